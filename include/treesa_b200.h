@@ -1,0 +1,163 @@
+/* treesa_b200.h -- C ABI of the B200 TreeSA annealer (libtreesa_b200.so).
+ *
+ * Drop-in replacement for the reference's process boundary: treesa_gpu/driver.py:215-314 writes an
+ * instance file, a tree file and a betas file, spawns the CLI binary (csrc/treesa_gpu.cu:2070-2086,
+ * options parsed at :1343-1406) and reads its JSON result (:1896-1919).  Here driver.optimize fills
+ * the structs below and makes one ctypes call; the result struct carries every JSON key.
+ *
+ * Conventions shared with the reference:
+ *   - leaves are tensors 0..m-1, internal nodes m..2m-2, the root is 2m-2 (csrc/treesa_gpu.cu:15-20);
+ *   - a tree is m-1 words, word i = left | right << 16 for internal node m+i (read_trees, :1077-1097);
+ *   - labels are 0..nlab-1 (driver.label_map, driver.py:60-67);
+ *   - chain c of the whole run (rank offset included) uses Philox counter {v, sweep, c, 0}.
+ * Plain pointers and sizes only.  Every entry point returns 0 on success and a TSA_ERR_* code otherwise,
+ * with a message in err; no entry point calls exit().
+ */
+#ifndef TREESA_B200_H
+#define TREESA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TSA_ABI_VERSION 1
+
+enum {
+  TSA_OK = 0,
+  TSA_ERR_ARG = 1,         /* invalid instance / tree / option (reference: exit(1) in read_instance etc.) */
+  TSA_ERR_INVALID = 2,     /* final tree invalid or labels mismatch (reference exit code 2, :1922) */
+  TSA_ERR_CUDA = 3,        /* CUDA runtime error (reference: CK() -> exit(1), :55-62) */
+  TSA_ERR_UNSUPPORTED = 4, /* option not available in this build */
+  TSA_ERR_NOMEM = 5,       /* device or host allocation failed */
+  TSA_ERR_TIMEOUT = 6,     /* a bounded device wait ran out (error status from a kernel) */
+  TSA_ERR_COMM = 7         /* NCCL error in a multi-GPU run */
+};
+
+enum { TSA_MODE_TC = 0, TSA_MODE_GPU = 1, TSA_MODE_H100 = 2 };
+enum { TSA_SCHEME_INDEP = 0, TSA_SCHEME_PA = 1, TSA_SCHEME_TRUNC = 2 };
+enum { TSA_ORDER_PAR = 0, TSA_ORDER_PREORDER = 1 };
+
+/* Tensor network: ixs in CSR form (driver.write_instance, driver.py:70-77; read_instance,
+ * csrc/treesa_gpu.cu:1035-1073).  Labels inside one tensor must be distinct. */
+typedef struct tsa_instance {
+  int32_t m;                  /* tensors (leaves), >= 3, 2m-1 <= 65535 */
+  int32_t nlab;               /* labels 0..nlab-1 */
+  const int32_t* ix_offsets;  /* [m+1] */
+  const int32_t* ix_labels;   /* [ix_offsets[m]] */
+  int32_t niy;                /* open (output) labels */
+  const int32_t* iy;          /* [niy] */
+} tsa_instance;
+
+/* Run options: every field of the reference's Opts (csrc/treesa_gpu.cu:1279-1298) that changes the
+ * result, plus placement.  Kernel-tuning options of the reference (kernel, wpb, lpc, coop_*, wpc,
+ * block, chunk_sums, wide) have no counterpart: the kernel choice here never changes a result. */
+typedef struct tsa_options {
+  const float* betas;         /* inverse temperatures, already expanded (parse_betas, :1305-1336) */
+  int32_t nbetas;
+  int32_t niters;             /* sweeps per beta level */
+  int32_t nchains;            /* chains of this call (this rank's shard when world_size > 1) */
+  int32_t mode;               /* TSA_MODE_TC (energy modes 1/2 are not built: TSA_ERR_UNSUPPORTED) */
+  double sc_target, sc_weight;
+  int32_t scheme;             /* TSA_SCHEME_* */
+  double trunc_frac;
+  int32_t order;              /* TSA_ORDER_* */
+  uint64_t seed;
+  int32_t eval_every;
+  int32_t slicing;            /* 0/1 */
+  int32_t slice_moves, slice_every, max_slices;
+  const int32_t* init_slices; /* labels sliced initially in every chain (--init-slices) */
+  int32_t ninit_slices;
+  int32_t select_sc;          /* --select-sc */
+  const uint32_t* init_trees; /* ntrees * (m-1) words; chain c starts from tree c % ntrees; NULL: random */
+  int32_t ntrees;
+  const double* gpu_model;    /* 6 values (peak_ops, bw_bits, m0, n0, k0, launch) or NULL: defaults */
+  const double* h100_model;   /* 9 values (launch, perm_bw_bits, cc_bit, cc_cell, tc_bit, tc_pad_cell,
+                                 tc_out_bit, small_rank, small_cell) or NULL: defaults */
+  int32_t device;             /* CUDA device ordinal */
+  void* stream;               /* cudaStream_t to launch on, or NULL: the library's own stream */
+  int32_t rank, world_size;   /* multi-GPU: one process per GPU; chains are sharded by rank */
+  const void* nccl_id;        /* 128-byte ncclUniqueId shared by all ranks (NULL when world_size == 1) */
+  int32_t verbose;
+  int32_t max_levels;         /* --max-levels (<= 0: all) */
+  int32_t reserved[14];
+} tsa_options;
+
+/* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the
+ * reference's output (csrc/treesa_gpu.cu:1896-1919). */
+typedef struct tsa_result {
+  int32_t m;
+  uint32_t* tree;             /* [m-1] words left | right << 16 */
+  int32_t nsliced;
+  int32_t* sliced;            /* [nsliced] label ids */
+  double tc, gpu_time, h100_time;   /* per slice, double precision (host_energy, :1206-1244) */
+  int32_t sc;
+  int32_t valid, labels_ok;
+  int32_t best_chain;         /* global chain id */
+  int32_t slicing, n_repair;
+  double tc_total, gpu_time_total, h100_time_total;
+  double t_anneal, t_init, kernel_s;
+  uint64_t proposals, accepts, warp_steps, node_visits, slice_proposals, slice_accepts, busy_lanes;
+  int32_t nchains, niters, nlevels, total_sweeps, W, nw, scheme, mode, nresample, order;
+  int32_t ntrace;
+  double* trace;              /* [ntrace][10]: t, level, beta, best_lcost_per_slice, best_sc, mean_E,
+                                 families, mode, best_nsliced, mean_nsliced (:1916) */
+  char kernel[32];
+  int32_t reserved[16];
+} tsa_result;
+
+/* TSA_ABI_VERSION of the loaded library. */
+int tsa_abi_version(void);
+
+/* One annealing run (reference: the whole CLI run, Runner<W>::run_anneal, :1756-1923).
+ * Replaces driver.py:215-314.  Thread-safe; concurrent calls on different devices run in parallel. */
+int tsa_run(const tsa_instance* inst, const tsa_options* opt, tsa_result* res, char* err, size_t errlen);
+
+/* Free the buffers of a result filled by tsa_run / tsa_session_result. */
+void tsa_result_free(tsa_result* res);
+
+/* Session API: tsa_run split into its phases, so that a caller can keep the chains resident on the
+ * device and time the anneal alone (bench), or re-run it from the same initial state.
+ *   create : validate, build the initial chains on the host, upload (reference: alloc + init_chains,
+ *            :1564-1630)
+ *   run    : every beta level: sweeps, energies, best tracking, resampling (:1789-1877)
+ *   result : finalize (labels check, greedy repair, host energies; :1878-1919)
+ *   reset  : restore the initial chains (device copy) and clear the run state */
+typedef struct tsa_session tsa_session;
+int tsa_session_create(const tsa_instance* inst, const tsa_options* opt, tsa_session** out, char* err,
+                       size_t errlen);
+int tsa_session_run(tsa_session* s, char* err, size_t errlen);
+int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen);
+int tsa_session_reset(tsa_session* s, char* err, size_t errlen);
+void tsa_session_destroy(tsa_session* s);
+
+/* Per-run counters of the last tsa_session_run: [0] proposals, [1] accepts, [2] phases (warp steps),
+ * [3] node visits, [4] slice proposals, [5] slice accepts, [6] busy lanes, [7] kernel launches,
+ * [8] 16-byte label chunks the moves touched; and the summed device time of the sweep kernels. */
+int tsa_session_stats(tsa_session* s, uint64_t* counters9, double* kernel_seconds);
+
+/* Energies of every chain after the last evaluated level (lcost per slice, sc, |S|), for tests. */
+int tsa_session_energies(tsa_session* s, float* lcost, int32_t* sc, int32_t* ns, char* err, size_t errlen);
+
+/* Copy the current chain trees ([nchains][m-1] words) and packed label sets ([nchains][m-1][nw] u64)
+ * to host buffers (either may be NULL), for tests. */
+int tsa_session_chains(tsa_session* s, uint32_t* trees, uint64_t* labels, char* err, size_t errlen);
+
+/* Multi-GPU rendezvous: write a fresh 128-byte ncclUniqueId into id (rank 0 calls it and shares the
+ * bytes with the other ranks, e.g. through torch.distributed). */
+int tsa_nccl_unique_id(void* id128, char* err, size_t errlen);
+
+/* Transfer plan of one population-resampling step on rank `rank` of `world` (nloc chains per rank,
+ * anc[g] = ancestor of global chain g): src_of[nloc] indexes [local records ++ received records];
+ * send_off[world+1]/send_idx[nloc*world]: local chains sent to each rank; recv_off[world+1]/
+ * recv_ids[nloc]: global chains received from each rank.  Host-only; exported for tests.
+ * No counterpart in the reference (single GPU, csrc/treesa_gpu.cu:1925-1933 copies in place). */
+int tsa_resample_plan(const int* anc, int nloc, int rank, int world, int* src_of, int* send_off, int* send_idx,
+                      int* recv_off, int* recv_ids);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TREESA_B200_H */

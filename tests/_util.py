@@ -1,0 +1,50 @@
+"""Shared helpers of the test suite: golden fixtures and instance packing."""
+import functools
+import json
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLDEN = os.path.join(HERE, "golden")
+
+
+@functools.lru_cache(None)
+def golden():
+    with open(os.path.join(GOLDEN, "instances.json")) as f:
+        inst = json.load(f)
+    with open(os.path.join(GOLDEN, "expected.json")) as f:
+        exp = json.load(f)
+    return inst, exp
+
+
+def instance(name):
+    return golden()[0][name]
+
+
+def words(tree):
+    t = np.asarray(tree, np.int64).reshape(-1, 2)
+    return (t[:, 0] | (t[:, 1] << 16)).astype(np.uint32)
+
+
+def julia_betas(a=0.01, st=0.05, e=15.0):
+    """Julia range a:st:e as float32 (driver.julia_betas, then the binary's float conversion)."""
+    n = int(np.floor((e - a) / st + 1e-9)) + 1
+    return np.array([a + i * st for i in range(n)], np.float32)
+
+
+def start_trees(rec, nchains, seed):
+    """Chains 0..nchains/2-1 from the greedy tree, the rest random (the host's random_tree stream)."""
+    import oracle as O
+    m = rec["m"]
+    g = words(rec["tree"])
+    half = nchains // 2
+    return np.stack([g] * half + [O.random_tree(m, seed, c) for c in range(half, nchains)])
+
+
+def digest(trees, labels):
+    import hashlib
+    h = hashlib.sha256()
+    h.update(np.ascontiguousarray(trees, np.uint32).tobytes())
+    h.update(np.ascontiguousarray(labels, np.uint64).tobytes())
+    return h.hexdigest()

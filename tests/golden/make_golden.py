@@ -1,0 +1,121 @@
+"""Generate the golden fixtures of the test suite from the reference (run in a container where the
+reference tree is mounted; the fixtures are committed and the GPU box never reads the reference).
+
+    python tests/golden/make_golden.py [REFERENCE_ROOT]
+
+Writes
+  instances.json  -- instances of the reference's tests/data (binary instance format, read_instance
+                     semantics) with their greedy start trees (*.tree, the omeco GreedyMethod trees of
+                     the reference's tests) and, where present, the multi-tree start files (*_multi.tree)
+  expected.json   -- (a) end-to-end tc/sc of the reference's logged Python test run
+                     (tests/test_python_results.txt: order par; tests/test_python_results_preorder.txt:
+                     order preorder; nchains 128, niters 4, sc_target 30, seed 1, betas 0.01:0.05:15);
+                     (b) SHA-256 of the final trees + labels that the reference's own csrc/cpu_ref.h
+                     (compiled from its sources by oracle/Makefile) produces on the run_checks.sh
+                     schedule (48 chains, betas 0.2:0.7:7, 4 sweeps, sc_target 24, seed 7), chains
+                     0..3 from the greedy tree, 4..7 random;
+                     (c) the sq32/sq48 row-major-start results of the reference's large-network
+                     benchmark log (bench/results/large_compare_gpu_par.jsonl), par order.
+"""
+import hashlib
+import json
+import os
+import re
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+INSTANCES = ["sat40", "sat60", "sat100", "reg3_100", "reg3_250", "lat10", "lat14", "grid24", "grid28", "sq46"]
+
+
+def read_instance(path):
+    tok = open(path).read().split()
+    m, nlab = int(tok[0]), int(tok[1])
+    k, ixs = 2, []
+    for _ in range(m):
+        n = int(tok[k])
+        ixs.append([int(x) for x in tok[k + 1:k + 1 + n]])
+        k += 1 + n
+    ny = int(tok[k]) if k < len(tok) else 0
+    iy = [int(x) for x in tok[k + 1:k + 1 + ny]]
+    return m, nlab, ixs, iy
+
+
+def read_trees(path, m):
+    v = np.array(open(path).read().split(), np.int64).reshape(-1, 2)
+    return v.reshape(-1, m - 1, 2).tolist()
+
+
+def julia_betas(a, st, e):
+    n = int(np.floor((e - a) / st + 1e-9)) + 1
+    return [a + i * st for i in range(n)]
+
+
+def tree_words(t):
+    t = np.asarray(t, np.int64)
+    return (t[:, 0] | (t[:, 1] << 16)).astype(np.uint32)
+
+
+def digest(trees, labels):
+    h = hashlib.sha256()
+    h.update(np.ascontiguousarray(trees, np.uint32).tobytes())
+    h.update(np.ascontiguousarray(labels, np.uint64).tobytes())
+    return h.hexdigest()
+
+
+def main(ref):
+    import oracle as O
+    data = os.path.join(ref, "tests", "data")
+    inst = {}
+    for name in INSTANCES:
+        m, nlab, ixs, iy = read_instance(os.path.join(data, name + ".txt"))
+        rec = dict(m=m, nlab=nlab, ixs=ixs, iy=iy, tree=read_trees(os.path.join(data, name + ".tree"), m)[0])
+        mp = os.path.join(data, name + "_multi.tree")
+        if os.path.exists(mp):
+            rec["multi"] = read_trees(mp, m)
+        inst[name] = rec
+    with open(os.path.join(HERE, "instances.json"), "w") as f:
+        json.dump(inst, f, separators=(",", ":"))
+
+    # (a) logged end-to-end results of the reference's Python tests
+    e2e = []
+    for order, fn in (("par", "test_python_results.txt"), ("preorder", "test_python_results_preorder.txt")):
+        for line in open(os.path.join(ref, "tests", fn)):
+            mm = re.match(r"ok\s+(\S+) (indep|pa|trunc)\s+(greedy|random) tc\s+: .* tc ([\d.]+)==([\d.]+) sc (\d+)==",
+                          line)
+            if mm:
+                e2e.append(dict(instance=mm[1], order=order, scheme=mm[2], init=mm[3], tc=float(mm[4]),
+                                sc=int(mm[6])))
+
+    # (b) the reference's cpu_ref.h on the run_checks.sh schedule
+    betas = julia_betas(0.2, 0.7, 7.0)
+    cpuref = []
+    for name in INSTANCES:
+        rec = inst[name]
+        if rec["nlab"] > 4200:
+            continue
+        net = O.Net(rec["ixs"], rec["iy"], rec["nlab"])
+        trees = np.stack([tree_words(rec["tree"])] * 4 + [O.random_tree(net.m, 7, c) for c in range(4, 8)])
+        for order in ("par", "preorder"):
+            t, l, cnt, _ = O.ref_sweeps(net, trees, betas, 4, order=order, seed=7, sc_target=24.0)
+            cpuref.append(dict(instance=name, order=order, betas=[0.2, 0.7, 7.0], niters=4, seed=7, sc_target=24.0,
+                               nchains=8, proposals=int(cnt[0]), accepts=int(cnt[1]), sha256=digest(t, l)))
+
+    # (c) sq32 / sq48 from the row-major path tree (tc / sc identical on RTX 6000 and H100)
+    large = []
+    for line in open(os.path.join(ref, "bench", "results", "large_compare_gpu_par.jsonl")):
+        r = json.loads(line)
+        if r.get("init") == "sweep" and r.get("niters") == 20 and r["instance"] in ("sq32", "sq48", "sq64"):
+            large.append(dict(instance=r["instance"], nchains=r["nchains"], niters=r["niters"], beta0=r["beta0"],
+                              tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
+    with open(os.path.join(HERE, "expected.json"), "w") as f:
+        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large), f, indent=1)
+    print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,104 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle and the reference's own cpu_ref.h.
+
+* trajectories: final trees and label sets of every chain after a fixed schedule are bit-identical to
+  oracle/tsa_oracle.cpp, which is itself pinned to the reference's cpu_ref.h (tests/test_oracle.py);
+  the first 8 chains also reproduce the SHA-256 of cpu_ref.h's own output recorded in tests/golden;
+* end to end: tsa_run reproduces the tc / sc of the reference's logged test run for every
+  (instance, order, scheme, start) row; tc is compared to the log's 4 decimals (|d| < 5e-5);
+* energies: per-chain lcost within 1e-3 of the host double tc (the reference's own bound,
+  csrc/treesa_gpu.cu:2056), sc and |S| exact.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from tests import _util
+from treesa_gpu_b200 import engine
+
+pytestmark = pytest.mark.gpu
+
+CHECK_BETAS = np.array([0.2 + 0.7 * i for i in range(10)], np.float32)  # run_checks.sh: 0.2:0.7:7
+SMALL = ["sat40", "sat60", "sat100", "reg3_100", "reg3_250", "lat10", "lat14"]
+
+
+def _net(rec):
+    return engine.Network(rec["ixs"], rec["iy"], rec["nlab"]), O.Net(rec["ixs"], rec["iy"], rec["nlab"])
+
+
+def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None):
+    opts = dict(betas=betas, niters=niters, nchains=len(trees), sc_target=sc_target, order=order, seed=seed,
+                init_trees=trees)
+    if S is not None:
+        opts["init_slices"] = S
+    s = engine.Session(net, **opts)
+    s.run()
+    t, lab = s.chains()
+    st = s.stats()
+    s.close()
+    return t, lab, st
+
+
+@pytest.mark.parametrize("order", ["par", "preorder"])
+@pytest.mark.parametrize("name", SMALL)
+def test_trajectories_bit_exact(name, order):
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    trees = _util.start_trees(rec, 64, seed=7)
+    t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 4, order, 7, 24.0)
+    ot, olab, ocnt = O.sweeps(onet, trees, CHECK_BETAS, 4, order=order, seed=7, sc_target=24.0)
+    nw = onet.nw
+    assert (t == ot).all(), f"{(t != ot).any(1).sum()} chains differ"
+    assert (lab[:, :, :nw] == olab).all()
+    assert (lab[:, :, nw:] == 0).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
+    if order == "par":
+        assert st["phases"] == ocnt[2]
+
+
+@pytest.mark.parametrize("order", ["par", "preorder"])
+@pytest.mark.parametrize("name", SMALL)
+def test_matches_reference_cpu_ref_digest(name, order, golden):
+    exp = [e for e in golden[1]["cpuref"] if e["instance"] == name and e["order"] == order]
+    assert exp, "missing fixture"
+    e = exp[0]
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    trees = _util.start_trees(rec, 8, seed=7)
+    t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 4, order, 7, 24.0)
+    assert _util.digest(t, np.ascontiguousarray(lab[:, :, :onet.nw])) == e["sha256"]
+    assert st["proposals"] == e["proposals"] and st["accepts"] == e["accepts"]
+
+
+def _e2e_rows(golden, orders=("par", "preorder")):
+    return [r for r in golden[1]["e2e"] if r["order"] in orders]
+
+
+@pytest.mark.parametrize("row", range(48))
+def test_reference_logged_results(row, golden):
+    rows = _e2e_rows(golden)
+    r = rows[row]
+    rec = _util.instance(r["instance"])
+    net, _ = _net(rec)
+    opts = dict(betas=_util.julia_betas(), niters=4, nchains=128, sc_target=30.0, scheme=r["scheme"],
+                order=r["order"], seed=1)
+    if r["init"] == "greedy":
+        opts["init_trees"] = _util.words(rec["tree"])[None, :]
+    rc, d = engine.run(net, **opts)
+    assert rc == 0 and d["valid"] and d["labels_ok"]
+    assert d["sc"] == r["sc"] and abs(d["tc"] - r["tc"]) < 5e-5, (r, d["tc"], d["sc"])
+
+
+@pytest.mark.parametrize("name", ["sat60", "lat14", "reg3_250"])
+def test_energies_match_host(name):
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    trees = _util.start_trees(rec, 16, seed=3)
+    s = engine.Session(net, betas=CHECK_BETAS[:3], niters=2, nchains=16, sc_target=24.0, seed=3, init_trees=trees)
+    s.run()
+    lc, sc, ns = s.energies()
+    t, _ = s.chains()
+    s.close()
+    for c in range(16):
+        olc, osc, ons, tch, sch = O.energy(onet, t[c])
+        assert abs(float(lc[c]) - tch) < 1e-3 and sc[c] == sch == osc and ns[c] == ons == 0
+        assert abs(float(lc[c]) - olc) <= 4e-6 * max(1.0, abs(olc))

@@ -1,0 +1,1012 @@
+// tsa_host.cpp -- host side of libtreesa_b200.so: the C ABI (include/treesa_b200.h), chain
+// initialization, the beta-level scheduler with best-of-N / population annealing / truncation selection,
+// and the finalize step.  Follows the reference's Runner<W> (csrc/treesa_gpu.cu:1416-1933) in
+// semantics; all state lives in a session object (no global mutable state), so concurrent calls on
+// different devices are independent.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <omp.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <chrono>
+#include <functional>
+#include <mutex>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "../../include/treesa_b200.h"
+#include "tsa_comm.h"
+#include "tsa_core.h"
+#include "tsa_exp_table.h"
+#include "tsa_kernels.cuh"
+
+using tsa::Layout;
+
+namespace {
+
+void set_err(char* err, size_t n, const char* fmt, ...) {
+  if (!err || n == 0) return;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(err, n, fmt, ap);
+  va_end(ap);
+}
+
+#define CKR(x)                                                                                 \
+  do {                                                                                         \
+    cudaError_t e_ = (x);                                                                      \
+    if (e_ != cudaSuccess) {                                                                   \
+      set_err(err, errlen, "CUDA error %s at %s:%d", cudaGetErrorString(e_), __FILE__, __LINE__); \
+      return TSA_ERR_CUDA;                                                                     \
+    }                                                                                          \
+  } while (0)
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+uint64_t splitmix64(uint64_t x) {  // csrc/treesa_gpu.cu:1408-1413
+  x += 0x9E3779B97F4A7C15ULL;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBULL;
+  return x ^ (x >> 31);
+}
+
+inline uint32_t rup(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
+inline int popc(uint64_t x) { return __builtin_popcountll(x); }
+
+// ------------------------------------------------------------------------------------------------
+// Instance (read_instance semantics, csrc/treesa_gpu.cu:1035-1073)
+// ------------------------------------------------------------------------------------------------
+struct Inst {
+  int m = 0, nlab = 0, nw = 1;
+  std::vector<std::vector<int>> ixs;
+  std::vector<int> iy, total;
+  std::vector<char> in_iy;
+  std::vector<uint64_t> leaf;  // [m][nw]
+  int leaf_sc = 0;
+};
+
+int load_inst(const tsa_instance* I, Inst& S, char* err, size_t errlen) {
+  if (!I || !I->ix_offsets || (I->m > 0 && !I->ix_labels)) {
+    set_err(err, errlen, "null instance");
+    return TSA_ERR_ARG;
+  }
+  if (I->m < 3) {
+    set_err(err, errlen, "need at least 3 tensors");
+    return TSA_ERR_ARG;
+  }
+  if (2 * (long long)I->m - 1 > 65535) {
+    set_err(err, errlen, "too many tensors (node ids are 16-bit)");
+    return TSA_ERR_ARG;
+  }
+  if (I->nlab < 0 || I->nlab > 32767) {
+    set_err(err, errlen, "label count out of range");
+    return TSA_ERR_ARG;
+  }
+  S.m = I->m;
+  S.nlab = I->nlab;
+  int nw = (I->nlab + 63) / 64;
+  if (nw < 1) nw = 1;
+  if (nw > 1 && (nw & 1)) nw++;  // 16-byte aligned label sets
+  S.nw = nw;
+  S.ixs.assign(S.m, {});
+  S.total.assign(S.nlab, 0);
+  S.in_iy.assign(S.nlab, 0);
+  for (int i = 0; i < S.m; i++) {
+    int a = I->ix_offsets[i], b = I->ix_offsets[i + 1];
+    if (b < a) {
+      set_err(err, errlen, "bad ix offsets");
+      return TSA_ERR_ARG;
+    }
+    S.ixs[i].assign(I->ix_labels + a, I->ix_labels + b);
+    std::sort(S.ixs[i].begin(), S.ixs[i].end());
+    if (std::adjacent_find(S.ixs[i].begin(), S.ixs[i].end()) != S.ixs[i].end()) {
+      set_err(err, errlen, "repeated label inside one tensor is not supported");
+      return TSA_ERR_ARG;
+    }
+    for (int l : S.ixs[i]) {
+      if (l < 0 || l >= S.nlab) {
+        set_err(err, errlen, "label out of range");
+        return TSA_ERR_ARG;
+      }
+      S.total[l]++;
+    }
+    S.leaf_sc = std::max(S.leaf_sc, (int)S.ixs[i].size());
+  }
+  for (int j = 0; j < I->niy; j++) {
+    int l = I->iy[j];
+    if (l < 0 || l >= S.nlab) {
+      set_err(err, errlen, "open label out of range");
+      return TSA_ERR_ARG;
+    }
+    S.iy.push_back(l);
+    S.in_iy[l] = 1;
+  }
+  S.leaf.assign((size_t)S.m * nw, 0);
+  for (int i = 0; i < S.m; i++)
+    for (int l : S.ixs[i]) S.leaf[(size_t)i * nw + (l >> 6)] |= 1ull << (l & 63);
+  return TSA_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Trees and labels
+// ------------------------------------------------------------------------------------------------
+// Julia random_exprtree as in csrc/treesa_gpu.cu:1101-1123 (same std::mt19937_64 draws)
+std::vector<uint32_t> random_tree(int m, uint64_t seed) {
+  std::mt19937_64 rng(seed);
+  std::vector<uint32_t> ch(m - 1);
+  int next = m;
+  std::function<int(const std::vector<int>&)> build = [&](const std::vector<int>& xs) -> int {
+    const int n = (int)xs.size();
+    if (n == 1) return xs[0];
+    std::vector<char> mask(n);
+    int cnt = 0;
+    for (int i = 0; i < n; i++) {
+      mask[i] = (char)(rng() & 1);
+      cnt += mask[i];
+    }
+    if (cnt == 0 || cnt == n) {
+      int i = (int)(rng() % n);
+      mask[i] = !mask[i];
+    }
+    std::vector<int> a, b;
+    a.reserve(n);
+    b.reserve(n);
+    for (int i = 0; i < n; i++) (mask[i] ? a : b).push_back(xs[i]);
+    int l = build(a), r = build(b);
+    int v = next++;
+    ch[v - m] = (uint32_t)l | ((uint32_t)r << 16);
+    return v;
+  };
+  std::vector<int> all(m);
+  std::iota(all.begin(), all.end(), 0);
+  build(all);
+  return ch;
+}
+
+// Output labels of every internal node from the topology (the rule of labels_from_topology,
+// csrc/treesa_gpu.cu:1149-1172: l is an output of v iff it occurs in v's subtree and also outside it,
+// or is open).  Computed by closure: z(v) = (z(left) | z(right)) minus the labels that close at v,
+// i.e. whose occurrences all lie in v's subtree for the first time (the LCA of the occurrences, or the
+// parent of the only occurrence); open labels never close.  O(m * nw + sum of occurrences * depth).
+// Returns false if ch is not a binary tree over all 2m-1 nodes rooted at 2m-2.
+bool topo_labels(const Inst& I, const uint32_t* ch, uint64_t* lab) {
+  const int m = I.m, n = 2 * m - 1, nw = I.nw;
+  std::vector<int> parent(n, -1), depth(n, 0), order;
+  order.reserve(m - 1);
+  {
+    std::vector<char> seen(n, 0);
+    std::vector<int> st{n - 1};
+    int nseen = 0;
+    while (!st.empty()) {
+      int v = st.back();
+      st.pop_back();
+      if (v < 0 || v >= n || seen[v]) return false;
+      seen[v] = 1;
+      nseen++;
+      if (v >= m) {
+        order.push_back(v);
+        int l = (int)(ch[v - m] & 0xFFFFu), r = (int)(ch[v - m] >> 16);
+        for (int u : {l, r}) {
+          if (u < 0 || u >= n) return false;
+          if (!seen[u]) {
+            parent[u] = v;
+            depth[u] = depth[v] + 1;
+          }
+          st.push_back(u);
+        }
+      }
+    }
+    if (nseen != n) return false;
+  }
+  // closing node of every non-open label
+  std::vector<std::vector<int>> closes(m - 1);
+  std::vector<int> first(I.nlab, -1), lca(I.nlab, -1);
+  for (int t = 0; t < m; t++)
+    for (int l : I.ixs[t]) {
+      if (I.in_iy[l]) continue;
+      if (lca[l] < 0) {
+        lca[l] = t;
+        continue;
+      }
+      int a = lca[l], b = t;
+      while (depth[a] > depth[b]) a = parent[a];
+      while (depth[b] > depth[a]) b = parent[b];
+      while (a != b) a = parent[a], b = parent[b];
+      lca[l] = a;
+    }
+  for (int l = 0; l < I.nlab; l++) {
+    if (lca[l] < 0) continue;
+    int v = lca[l] < m ? parent[lca[l]] : lca[l];  // a single occurrence closes at its parent
+    closes[v - m].push_back(l);
+  }
+  for (int k = (int)order.size() - 1; k >= 0; k--) {
+    int v = order[k];
+    int l = (int)(ch[v - m] & 0xFFFFu), r = (int)(ch[v - m] >> 16);
+    const uint64_t* x = l < m ? &I.leaf[(size_t)l * nw] : lab + (size_t)(l - m) * nw;
+    const uint64_t* y = r < m ? &I.leaf[(size_t)r * nw] : lab + (size_t)(r - m) * nw;
+    uint64_t* z = lab + (size_t)(v - m) * nw;
+    for (int w = 0; w < nw; w++) z[w] = x[w] | y[w];
+    for (int q : closes[v - m]) z[q >> 6] &= ~(1ull << (q & 63));
+  }
+  return true;
+}
+
+// (cost, size) words of every internal node, on the network sliced by S
+void fill_cz(const Inst& I, const uint32_t* ch, const uint64_t* lab, const uint64_t* S, uint32_t* cz) {
+  const int m = I.m, nw = I.nw;
+  for (int i = 0; i < m - 1; i++) {
+    int l = (int)(ch[i] & 0xFFFFu), r = (int)(ch[i] >> 16);
+    const uint64_t* x = l < m ? &I.leaf[(size_t)l * nw] : lab + (size_t)(l - m) * nw;
+    const uint64_t* y = r < m ? &I.leaf[(size_t)r * nw] : lab + (size_t)(r - m) * nw;
+    const uint64_t* z = lab + (size_t)i * nw;
+    int Z = 0, K = 0;
+    for (int w = 0; w < nw; w++) {
+      uint64_t nm = ~S[w], zz = z[w] & nm;
+      Z += popc(zz);
+      K += popc(x[w] & y[w] & nm & ~zz);
+    }
+    cz[i] = ((uint32_t)(Z + K) << 16) | (uint32_t)Z;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Host double-precision energies, cost models and the slicer repair (csrc/treesa_gpu.cu:1174-1274)
+// ------------------------------------------------------------------------------------------------
+struct Models {
+  float lpeak, lbw, llaunch;
+  int m0, n0, k0;
+  float l3launch, lperm2, lcc_bit, lcc_cell, ltc_bit, ltc_pad, ltc_out, lsmall_cell;
+  int small_rank;
+};
+Models make_models(const double* gm_in, const double* hm_in) {  // Runner ctor, :1461-1475
+  static const double gm_def[6] = {11.9e15, 1.6e13, 6, 6, 8, 4e-6};
+  static const double hm_def[9] = {4e-6, 1.23e13, 5.44e-14, 7.68e-15, 6.37e-14, 2.02e-16, 1.77e-13, 14, 1e-12};
+  const double* gm = gm_in ? gm_in : gm_def;
+  const double* hm = hm_in ? hm_in : hm_def;
+  Models M;
+  M.lpeak = (float)log2(gm[0]);
+  M.lbw = (float)log2(gm[1]);
+  M.m0 = (int)gm[2];
+  M.n0 = (int)gm[3];
+  M.k0 = (int)gm[4];
+  M.llaunch = (float)log2(gm[5]);
+  M.l3launch = (float)log2(3 * hm[0]);
+  M.lperm2 = (float)log2(2 / hm[1]);
+  M.lcc_bit = (float)log2(hm[2]);
+  M.lcc_cell = (float)log2(hm[3]);
+  M.ltc_bit = (float)log2(hm[4]);
+  M.ltc_pad = (float)log2(hm[5]);
+  M.ltc_out = (float)log2(hm[6]);
+  M.small_rank = (int)hm[7];
+  M.lsmall_cell = (float)log2(hm[8]);
+  return M;
+}
+double gpu_time_d(int B, int M_, int N, int K, const Models& M) {
+  double ops = exp2((double)(1 + B + std::max(M_, M.m0) + std::max(N, M.n0) + std::max(K, M.k0)));
+  double bits = exp2((double)(B + M_ + K)) + exp2((double)(B + N + K)) + exp2((double)(B + M_ + N));
+  return std::max(ops / exp2((double)M.lpeak), bits / exp2((double)M.lbw)) + exp2((double)M.llaunch);
+}
+double h100_time_d(int B, int M_, int N, int K, const Models& M) {
+  auto e = [](float l) { return exp2((double)l); };
+  if (B + M_ + N <= M.small_rank) return e(M.lsmall_cell) * exp2((double)(B + M_ + N + K));
+  double a = exp2((double)(B + M_ + K)), b = exp2((double)(B + N + K)), c = exp2((double)(B + M_ + N));
+  double moved = a + b + c;
+  double perm = e(M.lperm2) * (a + b);
+  double best = e(M.lcc_bit) * moved + e(M.lcc_cell) * exp2((double)(B + M_ + N + K));
+  if (K >= 7 && std::max(M_, N) >= 5) {
+    double tc = e(M.ltc_bit) * moved +
+                e(M.ltc_pad) * exp2((double)(B + std::max(M_, 6) + std::max(N, 6) + std::max(K, 8))) +
+                e(M.ltc_out) * c;
+    best = std::min(best, tc);
+  }
+  return e(M.l3launch) + perm + best;
+}
+
+struct HostE {
+  double tc = 0, time = 0, time2 = 0;
+  int sc = 0, ns = 0;
+};
+HostE host_energy(const Inst& I, const Models& Mo, const uint64_t* lab, const uint32_t* ch, const uint64_t* S) {
+  const int nw = I.nw, m = I.m;
+  HostE E;
+  std::vector<uint64_t> nm(nw, ~0ull);
+  if (S)
+    for (int w = 0; w < nw; w++) {
+      nm[w] = ~S[w];
+      E.ns += popc(S[w]);
+    }
+  for (int i = 0; i < m; i++) {
+    int z = 0;
+    for (int w = 0; w < nw; w++) z += popc(I.leaf[(size_t)i * nw + w] & nm[w]);
+    E.sc = std::max(E.sc, z);
+  }
+  double mx = -1e300;
+  std::vector<double> tcs;
+  tcs.reserve(m - 1);
+  for (int i = 0; i < m - 1; i++) {
+    int l = (int)(ch[i] & 0xFFFFu), r = (int)(ch[i] >> 16);
+    const uint64_t* x = l >= m ? lab + (size_t)(l - m) * nw : &I.leaf[(size_t)l * nw];
+    const uint64_t* y = r >= m ? lab + (size_t)(r - m) * nw : &I.leaf[(size_t)r * nw];
+    const uint64_t* z = lab + (size_t)i * nw;
+    int B = 0, M_ = 0, N = 0, K = 0, sz = 0;
+    for (int w = 0; w < nw; w++) {
+      uint64_t a = x[w] & nm[w], b = y[w] & nm[w], c = z[w] & nm[w];
+      B += popc(a & b & c);
+      M_ += popc(a & ~b & c);
+      N += popc(~a & b & c);
+      K += popc(a & b & ~c);
+      sz += popc(c);
+    }
+    double t = B + M_ + N + K;
+    tcs.push_back(t);
+    mx = std::max(mx, t);
+    E.sc = std::max(E.sc, sz);
+    E.time += gpu_time_d(B, M_, N, K, Mo);
+    E.time2 += h100_time_d(B, M_, N, K, Mo);
+  }
+  double s = 0;
+  for (double t : tcs) s += exp2(t - mx);
+  E.tc = mx + log2(s);
+  return E;
+}
+
+// Julia TreeSASlicer rule as a final repair (:1248-1274): while sc > sc_target, slice the label that
+// occurs most often among the largest masked tensors (ties: lowest label id).
+int greedy_repair(const Inst& I, const uint64_t* lab, uint64_t* S, double sc_target) {
+  const int nw = I.nw, m = I.m;
+  int added = 0;
+  for (;;) {
+    int scmax = 0;
+    std::vector<int> sizes(2 * m - 1);
+    auto so = [&](int v) -> const uint64_t* { return v < m ? &I.leaf[(size_t)v * nw] : lab + (size_t)(v - m) * nw; };
+    for (int v = 0; v < 2 * m - 1; v++) {
+      const uint64_t* a = so(v);
+      int z = 0;
+      for (int w = 0; w < nw; w++) z += popc(a[w] & ~S[w]);
+      sizes[v] = z;
+      scmax = std::max(scmax, z);
+    }
+    if (scmax <= sc_target || scmax == 0) return added;
+    std::vector<int> freq(I.nlab, 0);
+    for (int v = 0; v < 2 * m - 1; v++)
+      if (sizes[v] == scmax) {
+        const uint64_t* a = so(v);
+        for (int w = 0; w < nw; w++) {
+          uint64_t x = a[w] & ~S[w];
+          while (x) {
+            int b = __builtin_ctzll(x);
+            x &= x - 1;
+            freq[w * 64 + b]++;
+          }
+        }
+      }
+    int best = (int)(std::max_element(freq.begin(), freq.end()) - freq.begin());
+    S[best >> 6] |= 1ull << (best & 63);
+    added++;
+  }
+}
+
+float lse_entry(int d) { return (float)log2(1.0 + exp2(-(double)d)); }  // :2075
+
+}  // namespace
+
+// ==================================================================================================
+// Session
+// ==================================================================================================
+struct tsa_session {
+  Inst I;
+  Layout L{};
+  tsa::LaunchPlan plan{};
+  // options (owned copies)
+  std::vector<float> betas;
+  int niters = 0, nchains = 0, scheme = 0, order = 0, eval_every = 1, slicing = 0, slice_moves = 0;
+  int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1;
+  double sc_target = 20, sc_weight = 1, trunc_frac = 0.25;
+  uint64_t seed = 1;
+  uint32_t key0 = 0, key1 = 0;
+  Models models{};
+  std::vector<uint64_t> S0;
+  int chain0 = 0, nglobal = 0;
+  // device
+  cudaStream_t st = nullptr;
+  bool own_stream = false;
+  uint8_t *d_rec = nullptr, *d_rec2 = nullptr, *d_init = nullptr;
+  uint64_t* d_leaf = nullptr;
+  float *d_lse = nullptr, *d_lc = nullptr;
+  int *d_sc = nullptr, *d_ns = nullptr, *d_anc = nullptr, *d_err = nullptr;
+  unsigned long long* d_stats = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  tsa::Comm* comm = nullptr;
+  float h_lse[64];
+  double t_init = 0;
+  // run state
+  bool ran = false;
+  double best_score = INFINITY, kernel_ms = 0, t_anneal = 0;
+  int best_chain = -1, best_level = -1, nresample = 0;
+  uint32_t sweep_ctr = 0;
+  std::vector<uint8_t> best;  // record of the best chain (host)
+  std::vector<double> trace;
+  std::vector<float> lc;
+  std::vector<int> sc, ns;
+  uint64_t stats[9] = {0};
+  uint64_t launches = 0;
+
+  ~tsa_session() {
+    if (device >= 0) cudaSetDevice(device);
+    cudaFree(d_rec);
+    cudaFree(d_rec2);
+    cudaFree(d_init);
+    cudaFree(d_leaf);
+    cudaFree(d_lse);
+    cudaFree(d_lc);
+    cudaFree(d_sc);
+    cudaFree(d_ns);
+    cudaFree(d_anc);
+    cudaFree(d_err);
+    cudaFree(d_stats);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (own_stream && st) cudaStreamDestroy(st);
+    delete comm;
+  }
+
+  double score(float l, int s, int n) const {  // :1737-1747
+    if (slicing) return (double)n + (double)l + 1000.0 * std::max(0.0, (double)s - sc_target);
+    if (select_sc) return 4096.0 * std::max(0.0, (double)s - sc_target) + (double)l;
+    double tc = (double)l;
+    if ((double)s <= sc_target || sc_weight <= 0) return tc;
+    double pen = log2(sc_weight) + (double)s + log2(1.0 - exp2(sc_target - (double)s));
+    double mx = std::max(tc, pen), mn = std::min(tc, pen);
+    return mx + log2(1.0 + exp2(mn - mx));
+  }
+  double energyE(float l, int s, int n) const {  // :1750-1753
+    return (double)n + (double)l + sc_weight * std::max(0.0, (double)s - sc_target);
+  }
+};
+
+namespace {
+
+int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t errlen) {
+  CKR(cudaSetDevice(s->device));
+  if (O->stream) {
+    s->st = (cudaStream_t)O->stream;
+  } else {
+    CKR(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    s->own_stream = true;
+  }
+  if (tsa::plan_sweeps(s->L, s->nchains, s->device, &s->plan) != cudaSuccess) {
+    set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
+    return TSA_ERR_UNSUPPORTED;
+  }
+  const size_t recb = (size_t)s->L.rec_bytes * s->nchains;
+  CKR(cudaMalloc(&s->d_rec, recb));
+  CKR(cudaMalloc(&s->d_init, recb));
+  if (s->scheme != TSA_SCHEME_INDEP) CKR(cudaMalloc(&s->d_rec2, recb));
+  CKR(cudaMalloc(&s->d_leaf, s->I.leaf.size() * 8));
+  CKR(cudaMalloc(&s->d_lse, 64 * sizeof(float)));
+  CKR(cudaMalloc(&s->d_lc, s->nchains * sizeof(float)));
+  CKR(cudaMalloc(&s->d_sc, s->nchains * sizeof(int)));
+  CKR(cudaMalloc(&s->d_ns, s->nchains * sizeof(int)));
+  CKR(cudaMalloc(&s->d_anc, s->nchains * sizeof(int)));
+  CKR(cudaMalloc(&s->d_err, sizeof(int)));
+  CKR(cudaMalloc(&s->d_stats, 9 * sizeof(unsigned long long)));
+  CKR(cudaEventCreate(&s->ev0));
+  CKR(cudaEventCreate(&s->ev1));
+  CKR(cudaMemcpyAsync(s->d_leaf, s->I.leaf.data(), s->I.leaf.size() * 8, cudaMemcpyHostToDevice, s->st));
+  for (int d = 0; d < 64; d++) s->h_lse[d] = lse_entry(d);
+  CKR(tsa::upload_lse_table(s->h_lse, s->d_lse, s->st));
+  return TSA_OK;
+}
+
+// Build the initial chain records on the host (init_chains, csrc/treesa_gpu.cu:1585-1630) and upload.
+int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) {
+  const Inst& I = s->I;
+  const Layout& L = s->L;
+  const int nint = L.nint, nw = L.nw, K = O->init_trees ? O->ntrees : 0;
+  std::vector<uint8_t> host((size_t)L.rec_bytes * s->nchains, 0);
+  // distinct start trees: K given trees (chain c from tree c % K), else one random tree per chain
+  const int ndist = K > 0 ? std::min(K, s->nglobal) : s->nchains;
+  std::vector<std::vector<uint8_t>> recs(K > 0 ? ndist : 0);
+  int bad = 0;
+  auto build = [&](const uint32_t* tree, uint8_t* rec) -> bool {
+    uint64_t* lab = reinterpret_cast<uint64_t*>(rec);
+    uint32_t* ch = reinterpret_cast<uint32_t*>(rec + L.off_ch);
+    uint32_t* cz = reinterpret_cast<uint32_t*>(rec + L.off_cz);
+    uint64_t* S = reinterpret_cast<uint64_t*>(rec + L.off_S);
+    memcpy(ch, tree, (size_t)nint * 4);
+    memcpy(S, s->S0.data(), (size_t)nw * 8);
+    if (!topo_labels(I, ch, lab)) return false;
+    fill_cz(I, ch, lab, S, cz);
+    return true;
+  };
+  if (K > 0) {
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : bad)
+    for (int k = 0; k < ndist; k++) {
+      recs[k].assign(L.rec_bytes, 0);
+      if (!build(O->init_trees + (size_t)k * nint, recs[k].data())) bad++;
+    }
+    if (!bad)
+      for (int c = 0; c < s->nchains; c++)
+        memcpy(&host[(size_t)c * L.rec_bytes], recs[(s->chain0 + c) % K].data(), L.rec_bytes);
+  } else {
+#pragma omp parallel for schedule(dynamic, 4) reduction(+ : bad)
+    for (int c = 0; c < s->nchains; c++) {
+      uint64_t gc = (uint64_t)(s->chain0 + c);
+      std::vector<uint32_t> t = random_tree(I.m, splitmix64(s->seed * 1000003ULL + gc));
+      if (!build(t.data(), &host[(size_t)c * L.rec_bytes])) bad++;
+    }
+  }
+  if (bad) {
+    set_err(err, errlen, "invalid initial tree");
+    return TSA_ERR_ARG;
+  }
+  const size_t bytes = host.size();
+  CKR(cudaMemcpyAsync(s->d_init, host.data(), bytes, cudaMemcpyHostToDevice, s->st));
+  CKR(cudaMemcpyAsync(s->d_rec, s->d_init, bytes, cudaMemcpyDeviceToDevice, s->st));
+  CKR(cudaStreamSynchronize(s->st));
+  return TSA_OK;
+}
+
+int reset_run_state(tsa_session* s, char* err, size_t errlen) {
+  s->ran = false;
+  s->best_score = INFINITY;
+  s->best_chain = s->best_level = -1;
+  s->nresample = 0;
+  s->kernel_ms = 0;
+  s->t_anneal = 0;
+  s->sweep_ctr = 0;
+  s->best.clear();
+  s->trace.clear();
+  s->launches = 0;
+  memset(s->stats, 0, sizeof s->stats);
+  CKR(cudaMemsetAsync(s->d_stats, 0, 9 * sizeof(unsigned long long), s->st));
+  CKR(cudaMemsetAsync(s->d_err, 0, sizeof(int), s->st));
+  return TSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsa_abi_version(void) { return TSA_ABI_VERSION; }
+
+int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_session** out, char* err, size_t errlen) {
+  if (!out || !O) {
+    set_err(err, errlen, "null argument");
+    return TSA_ERR_ARG;
+  }
+  *out = nullptr;
+  double t0 = now_s();
+  tsa_session* s = new (std::nothrow) tsa_session();
+  if (!s) return TSA_ERR_NOMEM;
+  s->device = -1;
+  int rc = load_inst(inst, s->I, err, errlen);
+  if (rc) {
+    delete s;
+    return rc;
+  }
+  if (O->mode != TSA_MODE_TC) {
+    set_err(err, errlen, "energy modes gpu/h100 are not built in this version (mode tc only)");
+    delete s;
+    return TSA_ERR_UNSUPPORTED;
+  }
+  if (O->nchains < 1 || O->niters < 0 || O->nbetas < 1 || !O->betas) {
+    set_err(err, errlen, "need nchains >= 1, niters >= 0 and at least one beta");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  if (O->scheme < 0 || O->scheme > 2 || O->order < 0 || O->order > 1) {
+    set_err(err, errlen, "bad scheme or order");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  if (O->world_size < 1 || O->rank < 0 || O->rank >= O->world_size) {
+    set_err(err, errlen, "bad rank / world_size");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  if (O->init_trees && O->ntrees < 1) {
+    set_err(err, errlen, "init_trees given with ntrees < 1");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  const Inst& I = s->I;
+  s->betas.assign(O->betas, O->betas + O->nbetas);
+  if (O->max_levels > 0 && (int)s->betas.size() > O->max_levels) s->betas.resize(O->max_levels);
+  s->niters = O->niters;
+  s->nchains = O->nchains;
+  s->scheme = O->scheme;
+  s->order = O->order;
+  s->eval_every = std::max(1, O->eval_every);
+  s->slicing = O->slicing ? 1 : 0;
+  s->slice_moves = O->slicing ? std::max(0, O->slice_moves) : 0;
+  s->slice_every = std::max(1, O->slice_every);
+  s->max_slices = O->max_slices > 0 ? O->max_slices : I.nlab;
+  s->select_sc = O->select_sc ? 1 : 0;
+  s->verbose = O->verbose;
+  s->sc_target = O->sc_target;
+  s->sc_weight = O->sc_weight;
+  s->trunc_frac = O->trunc_frac;
+  s->seed = O->seed;
+  uint64_t k = splitmix64(O->seed);
+  s->key0 = (uint32_t)k;
+  s->key1 = (uint32_t)(k >> 32);
+  s->models = make_models(O->gpu_model, O->h100_model);
+  s->rank = O->rank;
+  s->world = O->world_size;
+  s->chain0 = O->rank * O->nchains;
+  s->nglobal = O->nchains * O->world_size;
+  s->device = O->device;
+  // layout
+  Layout& L = s->L;
+  L.m = I.m;
+  L.nint = I.m - 1;
+  L.nw = I.nw;
+  uint32_t lab_bytes = (uint32_t)L.nint * (uint32_t)L.nw * 8u;
+  L.off_ch = rup(lab_bytes, 16);
+  L.off_cz = L.off_ch + rup((uint32_t)L.nint * 4u, 16);
+  L.off_S = L.off_cz + rup((uint32_t)L.nint * 4u, 16);
+  L.rec_bytes = rup(L.off_S + (uint32_t)L.nw * 8u, 128);
+  s->S0.assign(L.nw, 0);
+  for (int j = 0; j < O->ninit_slices; j++) {
+    int l = O->init_slices[j];
+    if (l < 0 || l >= I.nlab) {
+      set_err(err, errlen, "bad init_slices label");
+      delete s;
+      return TSA_ERR_ARG;
+    }
+    s->S0[l >> 6] |= 1ull << (l & 63);
+    s->slicing = 1;
+  }
+  if (O->world_size > 1) {
+    rc = tsa::comm_create(O->nccl_id, O->rank, O->world_size, O->device, &s->comm, err, errlen);
+    if (rc) {
+      delete s;
+      return rc;
+    }
+  }
+  rc = init_device_state(s, O, err, errlen);
+  if (rc == TSA_OK) rc = init_chains(s, O, err, errlen);
+  if (rc == TSA_OK) rc = reset_run_state(s, err, errlen);
+  if (rc) {
+    delete s;
+    return rc;
+  }
+  s->t_init = now_s() - t0;
+  *out = s;
+  return TSA_OK;
+}
+
+void tsa_session_destroy(tsa_session* s) { delete s; }
+
+int tsa_session_reset(tsa_session* s, char* err, size_t errlen) {
+  if (!s) return TSA_ERR_ARG;
+  CKR(cudaSetDevice(s->device));
+  CKR(cudaMemcpyAsync(s->d_rec, s->d_init, (size_t)s->L.rec_bytes * s->nchains, cudaMemcpyDeviceToDevice, s->st));
+  int rc = reset_run_state(s, err, errlen);
+  if (rc) return rc;
+  CKR(cudaStreamSynchronize(s->st));
+  return TSA_OK;
+}
+
+// The beta-level loop (run_anneal, csrc/treesa_gpu.cu:1789-1877).
+int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
+  if (!s) return TSA_ERR_ARG;
+  if (s->ran) {
+    set_err(err, errlen, "session already ran: call tsa_session_reset first");
+    return TSA_ERR_ARG;
+  }
+  CKR(cudaSetDevice(s->device));
+  const int nch = s->nchains, ng = s->nglobal;
+  const size_t nlev = s->betas.size();
+  double t0 = now_s();
+  s->lc.assign(nch, 0.f);
+  s->sc.assign(nch, 0);
+  s->ns.assign(nch, 0);
+  std::vector<float> glc(ng);
+  std::vector<int> gsc(ng), gns(ng);
+  std::vector<int> family(ng), nfam(ng);
+  std::iota(family.begin(), family.end(), 0);
+  std::mt19937_64 hrng(splitmix64(s->seed + 777));
+  float beta_last = s->betas[0];
+  tsa::SweepArgs a{};
+  a.L = s->L;
+  a.leaf = s->d_leaf;
+  a.nchains = nch;
+  a.chain0 = s->chain0;
+  a.order = s->order;
+  a.nsweeps = s->niters;
+  a.sc_target = (float)s->sc_target;
+  a.sc_weight = (float)s->sc_weight;
+  a.key0 = s->key0;
+  a.key1 = s->key1;
+  a.slicing = s->slicing;
+  a.leaf_sc = s->I.leaf_sc;
+  a.slice_moves = s->slice_moves;
+  a.slice_every = s->slice_every;
+  a.max_slices = s->max_slices;
+  a.out_lc = s->d_lc;
+  a.out_sc = s->d_sc;
+  a.out_ns = s->d_ns;
+  a.stats = s->d_stats;
+  a.err = s->d_err;
+  a.lse_tab = s->d_lse;
+  for (size_t lev = 0; lev < nlev; lev++) {
+    a.recs = s->d_rec;
+    a.beta = s->betas[lev];
+    a.sweep0 = s->sweep_ctr;
+    CKR(cudaEventRecord(s->ev0, s->st));
+    CKR(tsa::launch_sweeps(a, s->plan, s->st));
+    CKR(cudaEventRecord(s->ev1, s->st));
+    s->launches++;
+    s->sweep_ctr += (uint32_t)s->niters;
+    const bool last = lev + 1 == nlev;
+    const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || last;
+    if (!eval) {
+      CKR(cudaEventSynchronize(s->ev1));
+      float ms = 0;
+      CKR(cudaEventElapsedTime(&ms, s->ev0, s->ev1));
+      s->kernel_ms += ms;
+      continue;
+    }
+    CKR(cudaMemcpyAsync(s->lc.data(), s->d_lc, nch * sizeof(float), cudaMemcpyDeviceToHost, s->st));
+    CKR(cudaMemcpyAsync(s->sc.data(), s->d_sc, nch * sizeof(int), cudaMemcpyDeviceToHost, s->st));
+    CKR(cudaMemcpyAsync(s->ns.data(), s->d_ns, nch * sizeof(int), cudaMemcpyDeviceToHost, s->st));
+    CKR(cudaStreamSynchronize(s->st));
+    {
+      float ms = 0;
+      CKR(cudaEventElapsedTime(&ms, s->ev0, s->ev1));
+      s->kernel_ms += ms;
+    }
+    int herr = 0;
+    CKR(cudaMemcpy(&herr, s->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) {
+      set_err(err, errlen, "a bounded device wait timed out (code %d)", herr);
+      return TSA_ERR_TIMEOUT;
+    }
+    // the whole population's energies (all ranks)
+    if (s->world > 1) {
+      int rc = s->comm->allgather_energies(s->d_lc, s->d_sc, s->d_ns, nch, glc.data(), gsc.data(), gns.data(), s->st,
+                                           err, errlen);
+      if (rc) return rc;
+    } else {
+      std::copy(s->lc.begin(), s->lc.end(), glc.begin());
+      std::copy(s->sc.begin(), s->sc.end(), gsc.begin());
+      std::copy(s->ns.begin(), s->ns.end(), gns.begin());
+    }
+    int bi = 0;
+    double bs = INFINITY, meanE = 0, meanNs = 0;
+    for (int c = 0; c < ng; c++) {
+      double sv = s->score(glc[c], gsc[c], gns[c]);
+      if (sv < bs) {
+        bs = sv;
+        bi = c;
+      }
+      meanE += s->energyE(glc[c], gsc[c], gns[c]);
+      meanNs += gns[c];
+    }
+    meanE /= ng;
+    meanNs /= ng;
+    if (bs < s->best_score) {
+      s->best_score = bs;
+      s->best_chain = bi;
+      s->best_level = (int)lev;
+      s->best.resize(s->L.rec_bytes);
+      int owner = bi / nch;
+      if (s->world > 1) {
+        int rc = s->comm->fetch_record(s->d_rec + (size_t)(bi % nch) * s->L.rec_bytes, s->L.rec_bytes, owner,
+                                       s->best.data(), s->st, err, errlen);
+        if (rc) return rc;
+      } else {
+        CKR(cudaMemcpyAsync(s->best.data(), s->d_rec + (size_t)bi * s->L.rec_bytes, s->L.rec_bytes,
+                            cudaMemcpyDeviceToHost, s->st));
+        CKR(cudaStreamSynchronize(s->st));
+      }
+    }
+    std::fill(nfam.begin(), nfam.end(), 0);
+    int nf = 0;
+    for (int c = 0; c < ng; c++)
+      if (nfam[family[c]]++ == 0) nf++;
+    double row[10] = {now_s() - t0, (double)lev, (double)s->betas[lev], (double)glc[bi], (double)gsc[bi], meanE,
+                      (double)nf, 0.0, (double)gns[bi], meanNs};
+    s->trace.insert(s->trace.end(), row, row + 10);
+    if (s->verbose && (lev % 25 == 0 || last))
+      fprintf(stderr, "lev %4zu beta %7.3f  best(l2cost/slice %.3f sc %d |S| %d)  meanE %.3f  families %d  t=%.2fs\n",
+              lev, s->betas[lev], (double)glc[bi], gsc[bi], gns[bi], meanE, nf, now_s() - t0);
+    if (last || s->scheme == TSA_SCHEME_INDEP) continue;
+    std::vector<int> anc(ng);
+    if (s->scheme == TSA_SCHEME_PA) {  // :1837-1856
+      double db = s->betas[lev + 1] - beta_last;
+      beta_last = s->betas[lev + 1];
+      std::vector<double> w(ng);
+      double Emin = INFINITY;
+      for (int c = 0; c < ng; c++) Emin = std::min(Emin, s->energyE(glc[c], gsc[c], gns[c]));
+      double wsum = 0;
+      for (int c = 0; c < ng; c++) {
+        w[c] = exp(-db * (s->energyE(glc[c], gsc[c], gns[c]) - Emin));
+        wsum += w[c];
+      }
+      double u = std::uniform_real_distribution<double>(0, 1)(hrng), acc = 0;
+      int j = 0;
+      for (int c = 0; c < ng; c++) {
+        acc += w[c] / wsum * ng;
+        while (j < ng && j + u < acc) anc[j++] = c;
+      }
+      while (j < ng) anc[j++] = ng - 1;
+    } else {  // truncation, :1857-1869
+      std::vector<int> idx(ng);
+      std::iota(idx.begin(), idx.end(), 0);
+      std::sort(idx.begin(), idx.end(), [&](int x, int y) {
+        return s->energyE(glc[x], gsc[x], gns[x]) < s->energyE(glc[y], gsc[y], gns[y]);
+      });
+      std::iota(anc.begin(), anc.end(), 0);
+      int nrep = (int)(s->trunc_frac * ng);
+      for (int q = 0; q < nrep; q++) anc[idx[ng - 1 - q]] = idx[q];
+    }
+    if (s->world > 1) {
+      int rc = s->comm->resample(anc.data(), s->d_rec, s->d_rec2, s->d_anc, nch, s->L.rec_bytes, s->st, err, errlen);
+      if (rc) return rc;
+    } else {
+      CKR(cudaMemcpyAsync(s->d_anc, anc.data(), nch * sizeof(int), cudaMemcpyHostToDevice, s->st));
+      CKR(tsa::launch_copy_chains(s->d_rec, s->d_rec2, s->d_anc, nch, s->L.rec_bytes, s->st));
+    }
+    std::swap(s->d_rec, s->d_rec2);
+    std::vector<int> nfm(ng);
+    for (int c = 0; c < ng; c++) nfm[c] = family[anc[c]];
+    family.swap(nfm);
+    s->nresample++;
+  }
+  CKR(cudaStreamSynchronize(s->st));
+  unsigned long long st[9];
+  CKR(cudaMemcpy(st, s->d_stats, sizeof st, cudaMemcpyDeviceToHost));
+  for (int q = 0; q < 9; q++) s->stats[q] = st[q];
+  s->stats[7] = s->launches;
+  if (s->world > 1) {
+    int rc = s->comm->sum_u64(s->stats, 7, s->st, err, errlen);
+    if (rc) return rc;
+  }
+  s->t_anneal = now_s() - t0;
+  s->ran = true;
+  return TSA_OK;
+}
+
+// Finalize (csrc/treesa_gpu.cu:1878-1919): labels check, greedy repair, host energies.
+int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen) {
+  if (!s || !res) return TSA_ERR_ARG;
+  memset(res, 0, sizeof *res);
+  if (!s->ran || s->best_chain < 0) {
+    set_err(err, errlen, "no completed run in this session");
+    return TSA_ERR_ARG;
+  }
+  const Inst& I = s->I;
+  const Layout& L = s->L;
+  const int nint = L.nint, nw = L.nw;
+  const uint64_t* blab = reinterpret_cast<const uint64_t*>(s->best.data());
+  const uint32_t* bch = reinterpret_cast<const uint32_t*>(s->best.data() + L.off_ch);
+  std::vector<uint64_t> S(reinterpret_cast<const uint64_t*>(s->best.data() + L.off_S),
+                          reinterpret_cast<const uint64_t*>(s->best.data() + L.off_S) + nw);
+  std::vector<uint64_t> lab2((size_t)nint * nw, 0);
+  bool valid = topo_labels(I, bch, lab2.data());
+  bool labels_ok = valid && memcmp(lab2.data(), blab, lab2.size() * 8) == 0;
+  int n_repair = 0;
+  if (s->slicing && valid) n_repair = greedy_repair(I, lab2.data(), S.data(), s->sc_target);
+  HostE HE = host_energy(I, s->models, lab2.data(), bch, s->slicing ? S.data() : nullptr);
+  res->m = I.m;
+  res->tree = (uint32_t*)malloc(sizeof(uint32_t) * std::max(1, nint));
+  memcpy(res->tree, bch, (size_t)nint * 4);
+  std::vector<int> sl;
+  if (s->slicing)
+    for (int l = 0; l < I.nlab; l++)
+      if (S[l >> 6] >> (l & 63) & 1ull) sl.push_back(l);
+  res->nsliced = (int)sl.size();
+  res->sliced = (int32_t*)malloc(sizeof(int32_t) * std::max<size_t>(1, sl.size()));
+  if (!sl.empty()) memcpy(res->sliced, sl.data(), sl.size() * 4);
+  res->tc = HE.tc;
+  res->sc = HE.sc;
+  res->gpu_time = HE.time;
+  res->h100_time = HE.time2;
+  res->valid = valid;
+  res->labels_ok = labels_ok;
+  res->best_chain = s->best_chain;
+  res->slicing = s->slicing;
+  res->n_repair = n_repair;
+  res->tc_total = HE.tc + HE.ns;
+  res->gpu_time_total = HE.time * exp2((double)HE.ns);
+  res->h100_time_total = HE.time2 * exp2((double)HE.ns);
+  res->t_anneal = s->t_anneal;
+  res->t_init = s->t_init;
+  res->kernel_s = s->kernel_ms / 1e3;
+  res->proposals = s->stats[0];
+  res->accepts = s->stats[1];
+  res->warp_steps = s->stats[2];
+  res->node_visits = (uint64_t)s->sweep_ctr * (uint64_t)s->nglobal * (uint64_t)nint;
+  res->slice_proposals = s->stats[4];
+  res->slice_accepts = s->stats[5];
+  res->busy_lanes = s->stats[6];
+  res->nchains = s->nglobal;
+  res->niters = s->niters;
+  res->nlevels = (int)s->betas.size();
+  res->total_sweeps = (int)s->sweep_ctr;
+  res->W = 0;
+  res->nw = nw;
+  res->scheme = s->scheme;
+  res->mode = TSA_MODE_TC;
+  res->nresample = s->nresample;
+  res->order = s->order;
+  res->ntrace = (int)(s->trace.size() / 10);
+  res->trace = (double*)malloc(sizeof(double) * std::max<size_t>(1, s->trace.size()));
+  if (!s->trace.empty()) memcpy(res->trace, s->trace.data(), s->trace.size() * 8);
+  snprintf(res->kernel, sizeof res->kernel, "%s", s->plan.kind == tsa::K_WARP ? "warp_smem" : "block_hbm");
+  return valid && labels_ok ? TSA_OK : TSA_ERR_INVALID;
+}
+
+void tsa_result_free(tsa_result* r) {
+  if (!r) return;
+  free(r->tree);
+  free(r->sliced);
+  free(r->trace);
+  r->tree = nullptr;
+  r->sliced = nullptr;
+  r->trace = nullptr;
+}
+
+int tsa_run(const tsa_instance* inst, const tsa_options* opt, tsa_result* res, char* err, size_t errlen) {
+  if (res) memset(res, 0, sizeof *res);
+  if (err && errlen) err[0] = 0;
+  tsa_session* s = nullptr;
+  int rc = tsa_session_create(inst, opt, &s, err, errlen);
+  if (rc) return rc;
+  rc = tsa_session_run(s, err, errlen);
+  if (rc == TSA_OK) rc = tsa_session_result(s, res, err, errlen);
+  if (rc == TSA_ERR_INVALID) set_err(err, errlen, "final tree invalid or labels mismatch");
+  tsa_session_destroy(s);
+  return rc;
+}
+
+int tsa_session_stats(tsa_session* s, uint64_t* c9, double* ksec) {
+  if (!s) return TSA_ERR_ARG;
+  if (c9)
+    for (int q = 0; q < 9; q++) c9[q] = s->stats[q];
+  if (ksec) *ksec = s->kernel_ms / 1e3;
+  return TSA_OK;
+}
+
+int tsa_session_energies(tsa_session* s, float* lcost, int32_t* sc, int32_t* ns, char* err, size_t errlen) {
+  if (!s) return TSA_ERR_ARG;
+  if ((int)s->lc.size() != s->nchains) {
+    set_err(err, errlen, "no energies yet");
+    return TSA_ERR_ARG;
+  }
+  if (lcost) memcpy(lcost, s->lc.data(), s->nchains * sizeof(float));
+  if (sc) memcpy(sc, s->sc.data(), s->nchains * sizeof(int));
+  if (ns) memcpy(ns, s->ns.data(), s->nchains * sizeof(int));
+  return TSA_OK;
+}
+
+int tsa_session_chains(tsa_session* s, uint32_t* trees, uint64_t* labels, char* err, size_t errlen) {
+  if (!s) return TSA_ERR_ARG;
+  CKR(cudaSetDevice(s->device));
+  const Layout& L = s->L;
+  std::vector<uint8_t> host((size_t)L.rec_bytes * s->nchains);
+  CKR(cudaMemcpyAsync(host.data(), s->d_rec, host.size(), cudaMemcpyDeviceToHost, s->st));
+  CKR(cudaStreamSynchronize(s->st));
+  for (int c = 0; c < s->nchains; c++) {
+    const uint8_t* rec = &host[(size_t)c * L.rec_bytes];
+    if (trees) memcpy(trees + (size_t)c * L.nint, rec + L.off_ch, (size_t)L.nint * 4);
+    if (labels) memcpy(labels + (size_t)c * L.nint * L.nw, rec, (size_t)L.nint * L.nw * 8);
+  }
+  return TSA_OK;
+}
+
+int tsa_nccl_unique_id(void* id128, char* err, size_t errlen) { return tsa::comm_unique_id(id128, err, errlen); }
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// tsa_kernels.cuh -- device-side layout and launch interface of the B200 TreeSA kernels.
+//
+// Chain record (one per chain, in HBM, 128-byte aligned, moved whole between HBM and shared memory by
+// bulk TMA copies):
+//   lab[nint][nw]  u64   unsliced output-label bitset of internal node m+i (label l = bit l%64 of word
+//                        l/64; nw = ceil(L/64), padded to even above 1 so a set is 16-byte aligned)
+//   ch[nint]       u32   left | right << 16 (node ids: leaves 0..m-1, internal m..2m-2, root 2m-2)
+//   cz[nint]       u32   cost << 16 | size of node m+i on the sliced network:
+//                        size = |z & ~S|, cost = size + |x & y & ~z & ~S| (x, y: children)
+//   S[nw]          u64   slice set
+// Leaf label sets (identical for every chain) are one shared table leaf[m][nw].
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tsa {
+
+struct Layout {
+  int m, nint, nw;           // leaves, internal nodes, u64 words per label set
+  uint32_t off_ch, off_cz, off_S, rec_bytes;
+};
+
+// Everything one sweep launch needs (passed by value).
+struct SweepArgs {
+  Layout L;
+  uint8_t* recs;             // [nchains] records of rec_bytes
+  const uint64_t* leaf;      // [m][nw]
+  int nchains, chain0;       // local chain count, global id of local chain 0
+  int order;                 // 0 par, 1 preorder
+  float beta;
+  uint32_t sweep0;
+  int nsweeps;
+  float sc_target, sc_weight;
+  uint32_t key0, key1;
+  int slicing, leaf_sc;
+  int slice_moves, slice_every, max_slices;
+  float* out_lc;             // [nchains] per-chain energy after the launch
+  int* out_sc;
+  int* out_ns;
+  unsigned long long* stats; // 9 counters (see tsa_session_stats)
+  int* err;                  // nonzero: a bounded wait timed out
+  const float* lse_tab;      // 64 floats (device)
+};
+
+// Kernel family chosen by the host for a layout.
+enum KernelKind { K_WARP = 0, K_BLOCK = 1 };
+
+struct LaunchPlan {
+  KernelKind kind;
+  int warps_per_cta;         // chains per CTA (K_WARP) or warps per chain (K_BLOCK)
+  int grid;
+  size_t smem;
+};
+
+// Host-side entry points (tsa_kernels.cu).
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, LaunchPlan* plan);
+cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
+cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
+                               cudaStream_t st);
+cudaError_t upload_lse_table(const float* host64, float* dev64, cudaStream_t st);
+int fixup_count();
+
+}  // namespace tsa
