@@ -1,0 +1,313 @@
+"""Benchmark of the TreeSA annealing sweep: node visits/s (BASELINE metric) on config C2.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+Workload: random 3-SAT n=100, m=426 (the reference's tests/data/sat100.txt,
+from tests/golden), spectral start (4 orderings), order par, sc_target 20, best-of-N, 4096 chains per GPU,
+betas 0.01:0.05:15 (300 levels) x 10 sweeps.  One step = one whole anneal of that workload.
+node visits = levels x sweeps x chains x (m-1) (reference bench/throughput.py:168).
+
+value: all ranks' visits / max-over-ranks device time of K steps, chains resident in HBM (session reset,
+       a device copy, starts each step); L2 (126 MB) flushed by a 256 MiB write between steps.
+e2e:   the same metric through the C ABI (tsa_run) from host buffers: host chain init, upload, anneal,
+       download and finalize inside the timed region.
+--impl reference: the reference's own CPU path (csrc/cpu_ref.h built into oracle/_ref) on all host cores.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "node visits/s"
+UNIT = "visits/s"
+
+
+def workload(nchains):
+    from tests import _util
+    rec = _util.instance("sat100")
+    return dict(rec=rec, nchains=nchains, betas=_util.julia_betas(0.01, 0.05, 15.0), niters=10, sc_target=20.0,
+                order="par", scheme="indep", seed=1)
+
+
+def config_dict(W, world):
+    return {"workload": "C2: random 3-SAT n=100 m=426 (sat100), spectral start, order par, tc/sc sc_target 20, "
+                        f"best-of-N, {W['nchains']} chains per GPU, betas 0.01:0.05:15 x {W['niters']} sweeps",
+            "instance": "sat100", "m": W["rec"]["m"], "labels": W["rec"]["nlab"], "chains_per_gpu": W["nchains"],
+            "levels": len(W["betas"]), "sweeps_per_level": W["niters"], "parallelism": f"chains sharded over {world} GPU(s)",
+            "l2": "flushed between steps (256 MiB write; population 42 MB is below L2)"}
+
+
+def start_trees(rec, seed=1):
+    from treesa_gpu_b200 import driver, engine, spectral
+    so = spectral.spectral_orders(rec["ixs"], rec["iy"], k=4, seed=seed)
+    return np.stack([engine.tree_words(driver.dict_to_children(spectral.path_tree(o), rec["m"])) for _, _, o in so])
+
+
+def visits_per_step(W, world):
+    return len(W["betas"]) * W["niters"] * W["nchains"] * world * (W["rec"]["m"] - 1)
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU: the reference's own cpu_ref.h (oracle/_ref), all host threads, bounded sample
+# ------------------------------------------------------------------------------------------------
+def cpu_reference_rate(W, trees, target_s=12.0):
+    import oracle as O
+    rec = W["rec"]
+    net = O.Net(rec["ixs"], rec["iy"], rec["nlab"])
+    kind = "reference" if O.cpuref() is not None else "port"
+    threads = os.cpu_count() or 1
+    nch = 2 * threads
+    start = np.stack([trees[c % len(trees)] for c in range(nch)])
+    betas = np.asarray(W["betas"], np.float32)
+
+    def run(nlev):
+        if kind == "reference":
+            t, l, cnt, secs = O.ref_sweeps(net, start, betas[:nlev], W["niters"], order=W["order"], seed=W["seed"],
+                                           sc_target=W["sc_target"], nthreads=threads)
+        else:
+            t0 = time.time()
+            O.sweeps(net, start, betas[:nlev], W["niters"], order=W["order"], seed=W["seed"], sc_target=W["sc_target"])
+            secs = time.time() - t0
+        return nch * nlev * W["niters"] * (net.m - 1), secs
+
+    v1, s1 = run(2)
+    nlev = int(max(2, min(len(betas), 2 * target_s / max(s1, 1e-3))))
+    v, s = run(nlev)
+    return dict(value=v / s, unit=UNIT, cores=threads, kind=kind,
+                sample=f"{nch} chains x first {nlev} of {len(betas)} levels x {W['niters']} sweeps "
+                       f"(sat100, spectral start, par), {s:.1f} s")
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ------------------------------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.p = None
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", gpu_id], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per launch of the sweep kernel from the committed ncu summary (None if absent)."""
+    p = os.path.join(ROOT, "profiles", "c2_sweep_ncu.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    return None
+
+
+# ------------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--chains", type=int, default=4096)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--levels", type=int, default=0, help="first L beta levels only (profiling runs)")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    W = workload(args.chains)
+    if args.levels > 0:
+        W["betas"] = W["betas"][:args.levels]
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        trees = start_trees(W["rec"])
+        for _ in range(args.warmup):
+            cpu_reference_rate(W, trees, target_s=4.0)
+        vals, t_total = [], 0.0
+        for _ in range(args.steps):
+            t0 = time.time()
+            r = cpu_reference_rate(W, trees, target_s=8.0)
+            t_total += time.time() - t0
+            vals.append(r["value"])
+        v = statistics.median(vals)
+        cb = dict(r, value=v)
+        line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+                "config": config_dict(W, 1), "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    from treesa_gpu_b200 import engine
+
+    rec = W["rec"]
+    net = engine.Network(rec["ixs"], rec["iy"], rec["nlab"])
+    trees = start_trees(rec)
+    nccl_id = None
+    if world > 1:
+        obj = [engine.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    stream = torch.cuda.current_stream()
+    opts = dict(betas=W["betas"], niters=W["niters"], nchains=W["nchains"], sc_target=W["sc_target"],
+                order=W["order"], scheme=W["scheme"], seed=W["seed"], init_trees=trees, device=local,
+                stream=stream.cuda_stream, rank=rank, world_size=world, nccl_id=nccl_id)
+    sess = engine.Session(net, **opts)
+    for _ in range(args.warmup):
+        sess.reset()
+        sess.run()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid) if hasattr(
+        torch.cuda.get_device_properties(local), "uuid") else str(local)
+    clk = Clocks(gpu_id)
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    kernel_s, launches, props, accs, visits_cnt = 0.0, 0, 0, 0, 0
+    for k in range(args.steps):
+        flush.zero_()
+        evs[k][0].record(stream)
+        sess.reset()
+        sess.run()
+        evs[k][1].record(stream)
+        st = sess.stats()
+        kernel_s += st["kernel_s"]
+        launches += st["launches"]
+        props += st["proposals"]
+        accs += st["accepts"]
+        visits_cnt += st["visits"]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = clk.stop()
+    t_rank = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    t = torch.tensor([t_rank, kernel_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    T, KS = float(t[0]), float(t[1])
+    rc, res = sess.result()
+    sess.close()
+    vps = visits_per_step(W, world)
+    value = args.steps * vps / T
+
+    # roofline of the dominant kernel (the sweep kernel): algorithmic bytes per visit (packed u64 bitsets)
+    nw64 = (rec["nlab"] + 63) // 64
+    bset = 8 * nw64
+    nint = rec["m"] - 1
+    lev_launches = launches  # one sweep launch per level per step (this rank)
+    alg = ((visits_cnt - props) * 4 + props * (8 + 5 * bset) + accs * (bset + 8)
+           + lev_launches * W["nchains"] * (nint * (3 * bset + 4) + bset))
+    peak, peak_kind = measured_peak()
+    achieved = alg / KS / 1e9  # GB/s over this rank's kernel time
+    trf = ncu_traffic()
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": trf, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+            else "fallback", "kernel_visits_per_s": world * W["nchains"] * len(W["betas"]) * W["niters"] * nint *
+            args.steps / KS, "kernel_s": KS, "launches_per_step": launches // args.steps}
+
+    # e2e through the C ABI with host buffers
+    e2e_t, h2d, d2h = 0.0, 0, 0
+    e2e_opts = dict(opts)
+    for k in range(args.e2e_steps + 1 if args.e2e_steps > 0 else 0):
+        if world > 1:
+            obj = [engine.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            e2e_opts["nccl_id"] = obj[0]
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        rc2, r2 = engine.run(net, **e2e_opts)
+        b.record(stream)
+        torch.cuda.synchronize()
+        if k > 0:  # the first call is a warm-up
+            e2e_t += a.elapsed_time(b) / 1e3
+            h2d += r2["h2d_bytes"]
+            d2h += r2["d2h_bytes"]
+    te = torch.tensor([e2e_t], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = args.e2e_steps * vps / float(te[0]) if args.e2e_steps > 0 else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_rate(W, trees)
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * T / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+                "config": config_dict(W, world),
+                "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.e2e_steps),
+                        "d2h_bytes_per_step": d2h // max(1, args.e2e_steps)},
+                "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+                "best_tc": res["tc"], "best_sc": res["sc"], "valid": bool(res["valid"] and res["labels_ok"])}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

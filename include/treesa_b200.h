@@ -82,7 +82,10 @@ typedef struct tsa_options {
   const void* nccl_id;        /* 128-byte ncclUniqueId shared by all ranks (NULL when world_size == 1) */
   int32_t verbose;
   int32_t max_levels;         /* --max-levels (<= 0: all) */
-  int32_t reserved[14];
+  int32_t exp_mode;           /* Metropolis expf: 0 = the host libm's (bit-exact with the reference's CPU port
+                                 csrc/cpu_ref.h, default); 1 = the device's expf (bit-exact with the
+                                 reference's GPU binary, csrc/common.h:228 compiled by nvcc) */
+  int32_t reserved[13];
 } tsa_options;
 
 /* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the
@@ -105,7 +108,8 @@ typedef struct tsa_result {
   double* trace;              /* [ntrace][10]: t, level, beta, best_lcost_per_slice, best_sc, mean_E,
                                  families, mode, best_nsliced, mean_nsliced (:1916) */
   char kernel[32];
-  int32_t reserved[16];
+  uint64_t h2d_bytes, d2h_bytes;  /* host<->device bytes the call copied (inputs, energies, best chains) */
+  int32_t reserved[12];
 } tsa_result;
 
 /* TSA_ABI_VERSION of the loaded library. */

@@ -4,7 +4,10 @@
   oracle/tsa_oracle.cpp, which is itself pinned to the reference's cpu_ref.h (tests/test_oracle.py);
   the first 8 chains also reproduce the SHA-256 of cpu_ref.h's own output recorded in tests/golden;
 * end to end: tsa_run reproduces the tc / sc of the reference's logged test run for every
-  (instance, order, scheme, start) row; tc is compared to the log's 4 decimals (|d| < 5e-5);
+  (instance, order, scheme, start) row; tc is compared to the log's 4 decimals (|d| < 5e-5).  The log
+  was made by the reference's GPU binary, whose Metropolis test calls the device's expf, so these runs
+  use exp_mode="device"; with the default exp_mode="host" (glibc expf, as csrc/cpu_ref.h) the run
+  equals the CPU oracle instead (test_host_exp_mode_equals_oracle);
 * energies: per-chain lcost within 1e-3 of the host double tc (the reference's own bound,
   csrc/treesa_gpu.cu:2056), sc and |S| exact.
 """
@@ -80,7 +83,7 @@ def test_reference_logged_results(row, golden):
     rec = _util.instance(r["instance"])
     net, _ = _net(rec)
     opts = dict(betas=_util.julia_betas(), niters=4, nchains=128, sc_target=30.0, scheme=r["scheme"],
-                order=r["order"], seed=1)
+                order=r["order"], seed=1, exp_mode="device")
     if r["init"] == "greedy":
         opts["init_trees"] = _util.words(rec["tree"])[None, :]
     rc, d = engine.run(net, **opts)
@@ -102,3 +105,21 @@ def test_energies_match_host(name):
         olc, osc, ons, tch, sch = O.energy(onet, t[c])
         assert abs(float(lc[c]) - tch) < 1e-3 and sc[c] == sch == osc and ns[c] == ons == 0
         assert abs(float(lc[c]) - olc) <= 4e-6 * max(1.0, abs(olc))
+
+
+@pytest.mark.parametrize("scheme", ["indep", "pa", "trunc"])
+@pytest.mark.parametrize("name", ["sat60", "lat10"])
+def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
+    """Default exp_mode: the whole run (selection included) follows the host libm; with best-of-N the
+    reported tree equals the oracle's (population steps depend on device-float energies, so for pa/trunc
+    only validity is asserted here)."""
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    kw = dict(betas=_util.julia_betas(0.01, 0.25, 6.0), niters=4, nchains=64, sc_target=30.0, scheme=scheme,
+              order="par", seed=2)
+    rc, d = engine.run(net, **kw)
+    assert rc == 0 and d["valid"] and d["labels_ok"]
+    if scheme == "indep":
+        orc, od = O.run(onet, **kw)
+        assert od["tree"] == d["tree"] and od["best_chain"] == d["best_chain"]
+        assert abs(od["tc"] - d["tc"]) < 1e-9 and od["sc"] == d["sc"]

@@ -38,7 +38,7 @@ class Options(C.Structure):
                 ("gpu_model", C.POINTER(C.c_double)), ("h100_model", C.POINTER(C.c_double)),
                 ("device", C.c_int32), ("stream", C.c_void_p), ("rank", C.c_int32), ("world_size", C.c_int32),
                 ("nccl_id", C.c_void_p), ("verbose", C.c_int32), ("max_levels", C.c_int32),
-                ("reserved", C.c_int32 * 14)]
+                ("exp_mode", C.c_int32), ("reserved", C.c_int32 * 13)]
 
 
 class Result(C.Structure):
@@ -54,7 +54,7 @@ class Result(C.Structure):
                 ("nlevels", C.c_int32), ("total_sweeps", C.c_int32), ("W", C.c_int32), ("nw", C.c_int32),
                 ("scheme", C.c_int32), ("mode", C.c_int32), ("nresample", C.c_int32), ("order", C.c_int32),
                 ("ntrace", C.c_int32), ("trace", C.POINTER(C.c_double)), ("kernel", C.c_char * 32),
-                ("reserved", C.c_int32 * 16)]
+                ("h2d_bytes", C.c_uint64), ("d2h_bytes", C.c_uint64), ("reserved", C.c_int32 * 12)]
 
 
 TRACE_COLS = ["t", "level", "beta", "best_lcost_per_slice", "best_sc", "mean_E", "families", "mode",
@@ -96,7 +96,8 @@ def pack_instance(ixs_ids, iy_ids, nlab, keep):
 def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, scheme="indep", trunc_frac=0.25,
                  order="par", seed=1, eval_every=1, slicing=False, slice_moves=1, slice_every=1, max_slices=0,
                  init_slices=(), select_sc=False, init_trees=None, gpu_model=None, h100_model=None, device=0,
-                 stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc"):
+                 stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc",
+                 exp_mode="host"):
     o = Options()
     o.betas, _ = keep.arr(np.asarray(betas, np.float32), np.float32, C.c_float)
     o.nbetas = len(betas)
@@ -136,6 +137,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
         o.nccl_id = C.cast(buf, C.c_void_p)
     o.verbose = int(bool(verbose))
     o.max_levels = int(max_levels)
+    o.exp_mode = {"host": 0, "device": 1}[exp_mode]
     return o
 
 
@@ -160,7 +162,8 @@ def result_to_dict(r):
              slice_accepts=int(r.slice_accepts), busy_lanes=int(r.busy_lanes), order=ORDER_NAME.get(r.order, "par"),
              nchains=int(r.nchains), niters=int(r.niters), nlevels=int(r.nlevels), total_sweeps=int(r.total_sweeps),
              W=int(r.W), nw=int(r.nw), kernel=r.kernel.decode(), scheme=SCHEME_NAME.get(r.scheme, "indep"),
-             mode=int(r.mode), nresample=int(r.nresample), trace_cols=list(TRACE_COLS), trace=trace, tree=tree)
+             mode=int(r.mode), nresample=int(r.nresample), trace_cols=list(TRACE_COLS), trace=trace, tree=tree,
+             h2d_bytes=int(r.h2d_bytes), d2h_bytes=int(r.d2h_bytes))
     return d
 
 

@@ -258,6 +258,16 @@ void fill_cz(const Inst& I, const uint32_t* ch, const uint64_t* lab, const uint6
   }
 }
 
+// chunk summaries of n label sets of nw words (bit c: words 2c, 2c+1 not both zero)
+void fill_sums(const uint64_t* lab, int n, int nw, uint64_t* out) {
+  for (int i = 0; i < n; i++) {
+    uint64_t s = 0;
+    for (int c = 0; c < nw / 2; c++)
+      if (lab[(size_t)i * nw + 2 * c] | lab[(size_t)i * nw + 2 * c + 1]) s |= 1ull << c;
+    out[i] = s;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------
 // Host double-precision energies, cost models and the slicer repair (csrc/treesa_gpu.cu:1174-1274)
 // ------------------------------------------------------------------------------------------------
@@ -409,7 +419,7 @@ struct tsa_session {
   // options (owned copies)
   std::vector<float> betas;
   int niters = 0, nchains = 0, scheme = 0, order = 0, eval_every = 1, slicing = 0, slice_moves = 0;
-  int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1;
+  int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1, exp_device = 0;
   double sc_target = 20, sc_weight = 1, trunc_frac = 0.25;
   uint64_t seed = 1;
   uint32_t key0 = 0, key1 = 0;
@@ -421,6 +431,7 @@ struct tsa_session {
   bool own_stream = false;
   uint8_t *d_rec = nullptr, *d_rec2 = nullptr, *d_init = nullptr;
   uint64_t* d_leaf = nullptr;
+  uint64_t* d_leaf_sum = nullptr;
   float *d_lse = nullptr, *d_lc = nullptr;
   int *d_sc = nullptr, *d_ns = nullptr, *d_anc = nullptr, *d_err = nullptr;
   unsigned long long* d_stats = nullptr;
@@ -439,6 +450,7 @@ struct tsa_session {
   std::vector<int> sc, ns;
   uint64_t stats[9] = {0};
   uint64_t launches = 0;
+  uint64_t h2d = 0, d2h = 0;  // bytes copied between host and device by this session
 
   ~tsa_session() {
     if (device >= 0) cudaSetDevice(device);
@@ -446,6 +458,7 @@ struct tsa_session {
     cudaFree(d_rec2);
     cudaFree(d_init);
     cudaFree(d_leaf);
+    cudaFree(d_leaf_sum);
     cudaFree(d_lse);
     cudaFree(d_lc);
     cudaFree(d_sc);
@@ -502,6 +515,14 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
   CKR(cudaEventCreate(&s->ev0));
   CKR(cudaEventCreate(&s->ev1));
   CKR(cudaMemcpyAsync(s->d_leaf, s->I.leaf.data(), s->I.leaf.size() * 8, cudaMemcpyHostToDevice, s->st));
+  {
+    std::vector<uint64_t> ls(s->I.m, 0);
+    if (s->L.sums) fill_sums(s->I.leaf.data(), s->I.m, s->L.nw, ls.data());
+    CKR(cudaMalloc(&s->d_leaf_sum, ls.size() * 8));
+    CKR(cudaMemcpy(s->d_leaf_sum, ls.data(), ls.size() * 8, cudaMemcpyHostToDevice));
+    s->h2d += ls.size() * 8;
+  }
+  s->h2d += s->I.leaf.size() * 8 + 64 * sizeof(float) + 64 * sizeof(double);
   for (int d = 0; d < 64; d++) s->h_lse[d] = lse_entry(d);
   CKR(tsa::upload_lse_table(s->h_lse, s->d_lse, s->st));
   return TSA_OK;
@@ -526,6 +547,7 @@ int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) 
     memcpy(S, s->S0.data(), (size_t)nw * 8);
     if (!topo_labels(I, ch, lab)) return false;
     fill_cz(I, ch, lab, S, cz);
+    if (L.sums) fill_sums(lab, nint, nw, reinterpret_cast<uint64_t*>(rec + L.off_sum));
     return true;
   };
   if (K > 0) {
@@ -551,6 +573,7 @@ int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) 
   }
   const size_t bytes = host.size();
   CKR(cudaMemcpyAsync(s->d_init, host.data(), bytes, cudaMemcpyHostToDevice, s->st));
+  s->h2d += bytes;
   CKR(cudaMemcpyAsync(s->d_rec, s->d_init, bytes, cudaMemcpyDeviceToDevice, s->st));
   CKR(cudaStreamSynchronize(s->st));
   return TSA_OK;
@@ -633,6 +656,12 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   s->max_slices = O->max_slices > 0 ? O->max_slices : I.nlab;
   s->select_sc = O->select_sc ? 1 : 0;
   s->verbose = O->verbose;
+  if (O->exp_mode < 0 || O->exp_mode > 1) {
+    set_err(err, errlen, "exp_mode must be 0 (host libm) or 1 (device expf)");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  s->exp_device = O->exp_mode;
   s->sc_target = O->sc_target;
   s->sc_weight = O->sc_weight;
   s->trunc_frac = O->trunc_frac;
@@ -655,7 +684,10 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   L.off_ch = rup(lab_bytes, 16);
   L.off_cz = L.off_ch + rup((uint32_t)L.nint * 4u, 16);
   L.off_S = L.off_cz + rup((uint32_t)L.nint * 4u, 16);
-  L.rec_bytes = rup(L.off_S + (uint32_t)L.nw * 8u, 128);
+  // chunk summaries (one u64 per node: 16-byte chunk c nonzero) for wide sets of 32..128 words
+  L.sums = (L.nw >= 32 && L.nw <= 128) ? 1 : 0;
+  L.off_sum = rup(L.off_S + (uint32_t)L.nw * 8u, 16);
+  L.rec_bytes = rup(L.off_sum + (L.sums ? (uint32_t)L.nint * 8u : 0u), 128);
   s->S0.assign(L.nw, 0);
   for (int j = 0; j < O->ninit_slices; j++) {
     int l = O->init_slices[j];
@@ -730,6 +762,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.key0 = s->key0;
   a.key1 = s->key1;
   a.slicing = s->slicing;
+  a.exp_device = s->exp_device;
   a.leaf_sc = s->I.leaf_sc;
   a.slice_moves = s->slice_moves;
   a.slice_every = s->slice_every;
@@ -740,6 +773,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.stats = s->d_stats;
   a.err = s->d_err;
   a.lse_tab = s->d_lse;
+  a.leaf_sum = s->d_leaf_sum;
   for (size_t lev = 0; lev < nlev; lev++) {
     a.recs = s->d_rec;
     a.beta = s->betas[lev];
@@ -762,6 +796,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     CKR(cudaMemcpyAsync(s->sc.data(), s->d_sc, nch * sizeof(int), cudaMemcpyDeviceToHost, s->st));
     CKR(cudaMemcpyAsync(s->ns.data(), s->d_ns, nch * sizeof(int), cudaMemcpyDeviceToHost, s->st));
     CKR(cudaStreamSynchronize(s->st));
+    s->d2h += (size_t)nch * (sizeof(float) + 2 * sizeof(int));
     {
       float ms = 0;
       CKR(cudaEventElapsedTime(&ms, s->ev0, s->ev1));
@@ -809,6 +844,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       } else {
         CKR(cudaMemcpyAsync(s->best.data(), s->d_rec + (size_t)bi * s->L.rec_bytes, s->L.rec_bytes,
                             cudaMemcpyDeviceToHost, s->st));
+        s->d2h += s->L.rec_bytes;
         CKR(cudaStreamSynchronize(s->st));
       }
     }
@@ -857,6 +893,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       if (rc) return rc;
     } else {
       CKR(cudaMemcpyAsync(s->d_anc, anc.data(), nch * sizeof(int), cudaMemcpyHostToDevice, s->st));
+      s->h2d += nch * sizeof(int);
       CKR(tsa::launch_copy_chains(s->d_rec, s->d_rec2, s->d_anc, nch, s->L.rec_bytes, s->st));
     }
     std::swap(s->d_rec, s->d_rec2);
@@ -946,6 +983,8 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
   res->trace = (double*)malloc(sizeof(double) * std::max<size_t>(1, s->trace.size()));
   if (!s->trace.empty()) memcpy(res->trace, s->trace.data(), s->trace.size() * 8);
   snprintf(res->kernel, sizeof res->kernel, "%s", s->plan.kind == tsa::K_WARP ? "warp_smem" : "block_hbm");
+  res->h2d_bytes = s->h2d;
+  res->d2h_bytes = s->d2h;
   return valid && labels_ok ? TSA_OK : TSA_ERR_INVALID;
 }
 

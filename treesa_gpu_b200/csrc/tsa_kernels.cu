@@ -131,6 +131,7 @@ struct WarpCtx {
   uint32_t key0, key1;
   float beta, sc_target, sc_weight;
   int slicing;
+  int exp_device;
   const float* lse;      // shared
   const double* exptab;  // shared: 2^(j/64)
   const uint64_t* leaf;  // shared
@@ -139,6 +140,18 @@ struct WarpCtx {
 struct Counters {
   unsigned long long prop, acc, steps, visits, sprop, sacc, busy;
 };
+
+// Metropolis: host-libm-exact (default) or with the device's expf as the reference's GPU binary
+__device__ __forceinline__ bool accept_rt(int exp_device, float beta, const double* exptab, uint32_t r, float dE) {
+  if (exp_device) {
+    float u = (float)(r >> 8) * (1.0f / 16777216.0f);
+    return u < expf(__fmul_rn(-beta, dE));
+  }
+  return metropolis(r, beta, dE, exptab, kExpfFixX, kExpfFixG, kExpfFixN);
+}
+__device__ __forceinline__ bool accept(const WarpCtx& X_, uint32_t r, float dE) {
+  return accept_rt(X_.exp_device, X_.beta, X_.exptab, r, dE);
+}
 
 // One TreeSA proposal at internal node v (one lane).  Semantics: csrc/cpu_ref.h:89-121 (Julia
 // optimize_subtree! at one node).  With P the pivot child (left for rules 0,1), O the other child,
@@ -184,7 +197,7 @@ __device__ __forceinline__ uint32_t visit(const WarpCtx& X_, uint64_t* lab, uint
   int cP1 = sx + k2, cV1 = sd + k3;
   float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, X_.sc_target, X_.sc_weight, X_.lse);
   cnt.prop++;
-  if (metropolis(rnd.y, X_.beta, dE, X_.exptab, kExpfFixX, kExpfFixG, kExpfFixN)) {
+  if (accept(X_, rnd.y, dE)) {
     cnt.acc++;
     stset<NW>(lab + (size_t)(Pn - m) * NW, Xs);
     cz[Pn - m] = ((uint32_t)cP1 << 16) | (uint32_t)sx;
@@ -349,7 +362,7 @@ __device__ void slice_step(const WarpCtx& X_, const SweepArgs& a, uint64_t* lab,
     EvalOut nxt = eval_cached<NW>(X_, cz2, S, a.leaf_sc, lane);
     float Enew = slice_energy(nxt, X_.sc_target, X_.sc_weight);
     cnt.sprop++;
-    if (metropolis(r2.x, X_.beta, __fsub_rn(Enew, Ecur), X_.exptab, kExpfFixX, kExpfFixG, kExpfFixN)) {
+    if (accept(X_, r2.x, __fsub_rn(Enew, Ecur))) {
       cnt.sacc++;
       cur = nxt;
       Ecur = Enew;
@@ -396,6 +409,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   X_.sc_target = a.sc_target;
   X_.sc_weight = a.sc_weight;
   X_.slicing = a.slicing;
+  X_.exp_device = a.exp_device;
   X_.lse = s_lse;
   X_.exptab = s_exp;
   X_.leaf = s_leaf;
@@ -562,6 +576,543 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   }
 }
 
+
+// ================================================================================================
+// k_anneal_block: one CTA per chain for chains that do not fit in shared memory.  Per-node metadata
+// (children, (cost, size), chunk summaries, priorities, parents, work lists) in shared memory; label
+// sets stay in HBM and are streamed in 16-byte chunks by G lanes per node (the reference's visit_coop,
+// csrc/treesa_gpu.cu:267-373, with u64 words and an exact integer cost cache).
+// ================================================================================================
+struct BlockSmem {
+  uint32_t off_ch, off_cz, off_cz2, off_sum, off_S, off_pri, off_par, off_wl, off_U, off_U2, total;
+  int nint2;
+  __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves) {
+    BlockSmem b;
+    b.nint2 = (int)rnd_up((uint32_t)L.nint, 8);
+    const uint32_t n2 = (uint32_t)b.nint2;
+    uint32_t o = 1024;  // [0,256) lse, [256,768) exp, [768,1024) block scalars
+    b.off_ch = o;
+    o += 4 * n2;
+    b.off_cz = o;
+    o += 4 * n2;
+    b.off_cz2 = o;
+    if (slice_moves > 0) o += 4 * n2;
+    b.off_sum = o;
+    if (L.sums) o += 8 * n2;
+    b.off_S = rnd_up(o, 16);
+    o = b.off_S + rnd_up(8u * (uint32_t)L.nw, 16);
+    b.off_pri = o;
+    o += 2 * n2;
+    b.off_par = o;
+    o += 2 * n2;
+    b.off_wl = o;
+    o += 2 * n2;
+    b.off_U = o;
+    o += 2 * n2;
+    b.off_U2 = o;
+    o += 2 * n2;
+    b.total = rnd_up(o, 128);
+    return b;
+  }
+};
+
+struct BlkCtx {
+  int m, nint, nw, nchunks;
+  uint32_t key0, key1;
+  float beta, sc_target, sc_weight;
+  int slicing, exp_device;
+  const float* lse;          // shared
+  const double* exptab;      // shared
+  const uint64_t* leaf;      // global [m][nw]
+  const uint64_t* leaf_sum;  // global [m]
+  uint64_t* lab;             // global: this chain's label sets
+  uint32_t* ch;              // shared
+  uint32_t* cz;              // shared
+  uint64_t* sum;             // shared (when sums)
+  uint64_t* S;               // shared copy of the slice set
+};
+
+__device__ __forceinline__ ulonglong2 ld2(const uint64_t* p) { return *reinterpret_cast<const ulonglong2*>(p); }
+
+// lanes t, t+G, ... of the set chunks of u (SUMS) or of all chunks
+template <bool SUMS, typename F>
+__device__ __forceinline__ void for_chunks(uint64_t u, int nchunks, int G, int t, F&& f) {
+  if (SUMS) {
+    int k = 0;
+    while (u) {
+      int c = __ffsll((long long)u) - 1;
+      u &= u - 1;
+      if ((k & (G - 1)) == t) f(c);
+      k++;
+    }
+  } else {
+    for (int c = t; c < nchunks; c += G) f(c);
+  }
+}
+
+template <bool SUMS, bool PAR>
+__device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
+                                           int G, int t, unsigned gm, Counters& cnt) {
+  const int m = B.m, i = v - m, nw = B.nw;
+  uint32_t chv = B.ch[i];
+  int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
+  bool li = l >= m, ri = r >= m;
+  if (!li && !ri) return;
+  U4 rnd = philox10((uint32_t)v, sweep, chain, 0u, B.key0, B.key1);
+  int rule = pick_rule(li, ri, rnd.x);
+  int slotP = rule >> 1;
+  int slotM = ((rule ^ (rule >> 1)) & 1) ^ 1;
+  int Pn = slotP ? r : l, On = slotP ? l : r;
+  uint32_t chp = B.ch[Pn - m];
+  int Mn = slotM ? (int)(chp >> 16) : (int)(chp & 0xFFFFu);
+  int Kn = slotM ? (int)(chp & 0xFFFFu) : (int)(chp >> 16);
+  const uint64_t* gD = B.lab + (size_t)i * nw;
+  uint64_t* gP = B.lab + (size_t)(Pn - m) * nw;
+  const uint64_t* gO = On >= m ? B.lab + (size_t)(On - m) * nw : B.leaf + (size_t)On * nw;
+  const uint64_t* gK = Kn >= m ? B.lab + (size_t)(Kn - m) * nw : B.leaf + (size_t)Kn * nw;
+  const uint64_t* gM = Mn >= m ? B.lab + (size_t)(Mn - m) * nw : B.leaf + (size_t)Mn * nw;
+  uint64_t u = ~0ull;
+  if (SUMS) {
+    auto so = [&](int n) { return n >= m ? B.sum[n - m] : B.leaf_sum[n]; };
+    u = B.sum[i] | so(On) | so(Kn) | so(Mn);
+  }
+  int sx = 0, k2 = 0, k3 = 0;
+  for_chunks<SUMS>(u, B.nchunks, G, t, [&](int c) {
+    ulonglong2 d = ld2(gD + 2 * c), o = ld2(gO + 2 * c), k = ld2(gK + 2 * c), mm = ld2(gM + 2 * c);
+    uint64_t n0 = ~0ull, n1 = ~0ull;
+    if (B.slicing) {
+      n0 = ~B.S[2 * c];
+      n1 = ~B.S[2 * c + 1];
+    }
+    uint64_t x0 = (k.x | o.x) & (mm.x | d.x), x1 = (k.y | o.y) & (mm.y | d.y);
+    uint64_t xm0 = x0 & n0, xm1 = x1 & n1;
+    sx += __popcll(xm0) + __popcll(xm1);
+    k2 += __popcll(k.x & o.x & ~x0 & n0) + __popcll(k.y & o.y & ~x1 & n1);
+    k3 += __popcll(xm0 & mm.x & ~d.x) + __popcll(xm1 & mm.y & ~d.y);
+  });
+  for (int off = G >> 1; off > 0; off >>= 1) {
+    sx += __shfl_xor_sync(gm, sx, off);
+    k2 += __shfl_xor_sync(gm, k2, off);
+    k3 += __shfl_xor_sync(gm, k3, off);
+  }
+  uint32_t czv = B.cz[i], czp = B.cz[Pn - m];
+  int sd = (int)(czv & 0xFFFFu), sp = (int)(czp & 0xFFFFu);
+  int cP1 = sx + k2, cV1 = sd + k3;
+  float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, B.sc_target, B.sc_weight, B.lse);
+  bool acc = accept_rt(B.exp_device, B.beta, B.exptab, rnd.y, dE);
+  if (t == 0) cnt.prop++;
+  if (!acc) return;
+  uint64_t xs = 0;
+  for_chunks<SUMS>(u, B.nchunks, G, t, [&](int c) {
+    ulonglong2 d = ld2(gD + 2 * c), o = ld2(gO + 2 * c), k = ld2(gK + 2 * c), mm = ld2(gM + 2 * c);
+    ulonglong2 x = make_ulonglong2((k.x | o.x) & (mm.x | d.x), (k.y | o.y) & (mm.y | d.y));
+    *reinterpret_cast<ulonglong2*>(gP + 2 * c) = x;
+    if (x.x | x.y) xs |= 1ull << c;
+  });
+  if (SUMS)
+    for (int off = G >> 1; off > 0; off >>= 1) xs |= __shfl_xor_sync(gm, xs, off);
+  __syncwarp(gm);
+  if (t == 0) {
+    cnt.acc++;
+    uint32_t nchp = slotM ? ((chp & 0xFFFFu) | ((uint32_t)On << 16)) : ((chp & 0xFFFF0000u) | (uint32_t)On);
+    uint32_t nchv = slotP ? ((chv & 0xFFFF0000u) | (uint32_t)Mn) : ((chv & 0xFFFFu) | ((uint32_t)Mn << 16));
+    B.ch[Pn - m] = nchp;
+    B.ch[i] = nchv;
+    B.cz[Pn - m] = ((uint32_t)cP1 << 16) | (uint32_t)sx;
+    B.cz[i] = ((uint32_t)cV1 << 16) | (uint32_t)sd;
+    if (SUMS) B.sum[Pn - m] = xs;
+    if (PAR) {
+      if (On >= m) par[On - m] = (uint16_t)Pn;
+      if (Mn >= m) par[Mn - m] = (uint16_t)v;
+    }
+  }
+}
+
+// Whole-chain energy from a (cost, size) cache, one warp, in the reference's lane order.
+__device__ EvalOut eval_cz(const uint32_t* cz, int nint, const uint64_t* S, int nw, const uint64_t* leaf, int m,
+                           int slicing, int leaf_sc, int lane) {
+  const unsigned FULL = 0xFFFFFFFFu;
+  float acc = -INFINITY;
+  int scl = 0, cntl = 0;
+  for (int i = lane; i < nint; i += 32) {
+    uint32_t w = cz[i];
+    int Z = (int)(w & 0xFFFFu);
+    acc = lse_f(acc, (float)(int)(w >> 16));
+    if (Z > scl) {
+      scl = Z;
+      cntl = 1;
+    } else if (Z == scl) {
+      cntl++;
+    }
+  }
+  int scmax = scl;
+  for (int o = 16; o > 0; o >>= 1) {
+    acc = lse_f(acc, __shfl_xor_sync(FULL, acc, o));
+    scmax = max(scmax, __shfl_xor_sync(FULL, scmax, o));
+  }
+  int cnt = (scl == scmax) ? cntl : 0, ns = 0;
+  if (slicing)
+    for (int w = lane; w < nw; w += 32) ns += __popcll(S[w]);
+  for (int o = 16; o > 0; o >>= 1) {
+    cnt += __shfl_xor_sync(FULL, cnt, o);
+    ns += __shfl_xor_sync(FULL, ns, o);
+  }
+  int sc = max(scmax, leaf_sc);
+  if (slicing && leaf_sc > scmax) {
+    int ll = 0;
+    for (int i = lane; i < m; i += 32) {
+      int Z = 0;
+      for (int w = 0; w < nw; w++) Z += __popcll(leaf[(size_t)i * nw + w] & ~S[w]);
+      ll = max(ll, Z);
+    }
+    for (int o = 16; o > 0; o >>= 1) ll = max(ll, __shfl_xor_sync(FULL, ll, o));
+    sc = max(scmax, ll);
+  }
+  return EvalOut{acc, sc, scmax, cnt, ns};
+}
+
+__device__ __forceinline__ int nth_label_rt(const uint64_t* A, const uint64_t* S, int nw, int n) {
+  for (int w = 0; w < nw; w++) {
+    uint64_t x = A[w] & (S ? ~S[w] : ~0ull);
+    int c = __popcll(x);
+    if (n < c) {
+      for (int k = 0; k < n; k++) x &= x - 1;
+      return w * 64 + __ffsll((long long)x) - 1;
+    }
+    n -= c;
+  }
+  return -1;
+}
+
+// Slice moves of one chain, the whole CTA cooperating (slice_step, csrc/treesa_gpu.cu:445-502):
+// warp 0 chooses and judges the proposals; all threads recompute the (cost, size) cache for the
+// proposed slice set.
+__device__ void slice_step_block(const BlkCtx& B, const SweepArgs& a, uint32_t* cz2, int* sh, float* shf,
+                                 uint32_t sweep, uint32_t chain, Counters& cnt) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, T = blockDim.x, m = B.m, nw = B.nw;
+  EvalOut cur{};
+  float Ecur = 0.f;
+  if (warp == 0) {
+    cur = eval_cz(B.cz, B.nint, B.S, nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+    Ecur = slice_energy(cur, B.sc_target, B.sc_weight);
+  }
+  for (int j = 0; j < a.slice_moves; j++) {
+    if (warp == 0) {
+      U4 r1 = philox10(0x10000u + 2u * j, sweep, chain, 0u, B.key0, B.key1);
+      int type;
+      if (cur.ns == 0) type = 0;
+      else if (cur.ns >= a.max_slices) type = (r1.x >> 31) ? 1 : 2;
+      else type = r1.x < 0x80000000u ? 0 : (r1.x < 0xC0000000u ? 1 : 2);
+      int ladd = -1, lrem = -1;
+      if (type != 1 && cur.ncand > 0 && cur.sc_int > 0) {
+        int rr = (int)(r1.y % (uint32_t)cur.ncand), node = -1;
+        for (int base = 0; base < B.nint && node < 0; base += 32) {
+          int i = base + lane;
+          int Z = i < B.nint ? (int)(B.cz[i] & 0xFFFFu) : -1;
+          unsigned bb = __ballot_sync(0xFFFFFFFFu, Z == cur.sc_int);
+          int c = __popc(bb);
+          if (rr < c) {
+            for (int k = 0; k < rr; k++) bb &= bb - 1;
+            node = base + __ffs(bb) - 1;
+          } else {
+            rr -= c;
+          }
+        }
+        if (node >= 0) ladd = nth_label_rt(B.lab + (size_t)node * nw, B.S, nw, (int)(r1.z % (uint32_t)cur.sc_int));
+      }
+      if (type != 0) lrem = nth_label_rt(B.S, nullptr, nw, (int)(r1.w % (uint32_t)cur.ns));
+      if (type == 2 && ladd < 0) type = 1;
+      int skip = (type == 0 && ladd < 0);
+      if (lane == 0) {
+        sh[0] = skip;
+        sh[1] = type;
+        sh[2] = ladd;
+        sh[3] = lrem;
+        if (!skip) {
+          if (type != 1) B.S[ladd >> 6] |= 1ull << (ladd & 63);
+          if (type != 0) B.S[lrem >> 6] &= ~(1ull << (lrem & 63));
+        }
+      }
+    }
+    __syncthreads();
+    if (sh[0]) {
+      __syncthreads();
+      continue;
+    }
+    for (int i = tid; i < B.nint; i += T) {
+      uint32_t cw = B.ch[i];
+      int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+      const uint64_t* px = l >= m ? B.lab + (size_t)(l - m) * nw : B.leaf + (size_t)l * nw;
+      const uint64_t* py = r >= m ? B.lab + (size_t)(r - m) * nw : B.leaf + (size_t)r * nw;
+      const uint64_t* pz = B.lab + (size_t)i * nw;
+      int Z = 0, K = 0;
+      for (int w = 0; w < nw; w++) {
+        uint64_t nm = ~B.S[w], zz = pz[w] & nm;
+        Z += __popcll(zz);
+        K += __popcll(px[w] & py[w] & nm & ~zz);
+      }
+      cz2[i] = ((uint32_t)(Z + K) << 16) | (uint32_t)Z;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      EvalOut nxt = eval_cz(cz2, B.nint, B.S, nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+      float Enew = slice_energy(nxt, B.sc_target, B.sc_weight);
+      U4 r2 = philox10(0x10001u + 2u * j, sweep, chain, 0u, B.key0, B.key1);
+      bool acc = accept_rt(B.exp_device, B.beta, B.exptab, r2.x, __fsub_rn(Enew, Ecur));
+      cnt.sprop++;
+      if (acc) {
+        cnt.sacc++;
+        cur = nxt;
+        Ecur = Enew;
+      }
+      if (lane == 0) sh[4] = acc;
+    }
+    __syncthreads();
+    if (sh[4]) {
+      for (int i = tid; i < B.nint; i += T) B.cz[i] = cz2[i];
+    } else if (tid == 0) {
+      int type = sh[1], ladd = sh[2], lrem = sh[3];
+      if (type != 1) B.S[ladd >> 6] &= ~(1ull << (ladd & 63));
+      if (type != 0) B.S[lrem >> 6] |= 1ull << (lrem & 63);
+    }
+    __syncthreads();
+  }
+  (void)shf;
+}
+
+__device__ __forceinline__ int pick_group(int k, int T) {
+  int G = 32;
+  while (G > 1 && k * G > T) G >>= 1;
+  return G;
+}
+
+template <bool SUMS, int ORDER>
+__global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const Layout L = a.L;
+  const BlockSmem Bm = BlockSmem::make(L, a.slice_moves);
+  const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned FULL = 0xFFFFFFFFu;
+  float* s_lse = reinterpret_cast<float*>(smem);
+  double* s_exp = reinterpret_cast<double*>(smem + 256);
+  int* sh = reinterpret_cast<int*>(smem + 768);  // block scalars
+  for (int q = tid; q < 64; q += T) {
+    s_lse[q] = a.lse_tab[q];
+    s_exp[q] = c_exp_tab[q];
+  }
+  BlkCtx B;
+  B.m = L.m;
+  B.nint = L.nint;
+  B.nw = L.nw;
+  B.nchunks = L.nw / 2;
+  B.key0 = a.key0;
+  B.key1 = a.key1;
+  B.beta = a.beta;
+  B.sc_target = a.sc_target;
+  B.sc_weight = a.sc_weight;
+  B.slicing = a.slicing;
+  B.exp_device = a.exp_device;
+  B.lse = s_lse;
+  B.exptab = s_exp;
+  B.leaf = a.leaf;
+  B.leaf_sum = a.leaf_sum;
+  B.ch = reinterpret_cast<uint32_t*>(smem + Bm.off_ch);
+  B.cz = reinterpret_cast<uint32_t*>(smem + Bm.off_cz);
+  B.sum = reinterpret_cast<uint64_t*>(smem + Bm.off_sum);
+  B.S = reinterpret_cast<uint64_t*>(smem + Bm.off_S);
+  uint32_t* cz2 = reinterpret_cast<uint32_t*>(smem + Bm.off_cz2);
+  uint16_t* pri = reinterpret_cast<uint16_t*>(smem + Bm.off_pri);
+  uint16_t* par = reinterpret_cast<uint16_t*>(smem + Bm.off_par);
+  uint16_t* wl = reinterpret_cast<uint16_t*>(smem + Bm.off_wl);
+  uint16_t* Ua = reinterpret_cast<uint16_t*>(smem + Bm.off_U);
+  uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
+  const int m = L.m, nint = L.nint;
+  const unsigned lt = (1u << lane) - 1u;
+  Counters cnt{};
+  __syncthreads();
+  for (int c = blockIdx.x; c < a.nchains; c += gridDim.x) {
+    uint8_t* grec = a.recs + (size_t)c * L.rec_bytes;
+    B.lab = reinterpret_cast<uint64_t*>(grec);
+    const uint32_t* gch = reinterpret_cast<const uint32_t*>(grec + L.off_ch);
+    const uint32_t* gcz = reinterpret_cast<const uint32_t*>(grec + L.off_cz);
+    const uint64_t* gS = reinterpret_cast<const uint64_t*>(grec + L.off_S);
+    for (int q = tid; q < nint; q += T) {
+      B.ch[q] = gch[q];
+      B.cz[q] = gcz[q];
+    }
+    if (SUMS) {
+      const uint64_t* gs = reinterpret_cast<const uint64_t*>(grec + L.off_sum);
+      for (int q = tid; q < nint; q += T) B.sum[q] = gs[q];
+    }
+    for (int q = tid; q < L.nw; q += T) B.S[q] = gS[q];
+    __syncthreads();
+    const uint32_t chain = (uint32_t)(a.chain0 + c);
+    const uint32_t hc = chain_hash(chain, a.key0);
+    if (ORDER == 0) {
+      for (int q = tid; q < nint; q += T) {
+        uint32_t cw = B.ch[q];
+        int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+        if (l >= m) par[l - m] = (uint16_t)(m + q);
+        if (r >= m) par[r - m] = (uint16_t)(m + q);
+      }
+      if (tid == 0) par[nint - 1] = 0xFFFFu;
+      __syncthreads();
+    }
+    for (int s = 0; s < a.nsweeps; s++) {
+      const uint32_t sw = a.sweep0 + (uint32_t)s;
+      if (ORDER == 0) {
+        const uint32_t hs = sweep_hash(sw, hc);
+        for (int q = tid; q < nint; q += T) {
+          pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
+          Ua[q] = (uint16_t)q;
+        }
+        uint16_t *U = Ua, *U2 = Ub;
+        int nU = nint;
+        for (int guard = 0; guard <= nint; guard++) {
+          if (tid == 0) {
+            sh[0] = 0;
+            sh[1] = 0;
+          }
+          __syncthreads();
+          for (int base = 0; base < nU; base += T) {
+            int j = base + tid;
+            bool valid = j < nU;
+            int q = valid ? (int)U[j] : 0;
+            bool act = false;
+            if (valid) {
+              uint32_t key = ((uint32_t)pri[q] << 16) | (uint32_t)(m + q);
+              act = true;
+              int p = par[q];
+              if (p != 0xFFFF) {
+                uint32_t pp = pri[p - m];
+                if (pp && ((pp << 16) | (uint32_t)p) > key) act = false;
+              }
+              uint32_t cw = B.ch[q];
+              int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+              if (act && l >= m) {
+                uint32_t pl = pri[l - m];
+                if (pl && ((pl << 16) | (uint32_t)l) > key) act = false;
+              }
+              if (act && r >= m) {
+                uint32_t pr = pri[r - m];
+                if (pr && ((pr << 16) | (uint32_t)r) > key) act = false;
+              }
+            }
+            unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
+            int pa = 0, pk = 0;
+            if (lane == 0) {
+              if (ba) pa = atomicAdd(&sh[0], __popc(ba));
+              if (bk) pk = atomicAdd(&sh[1], __popc(bk));
+            }
+            pa = __shfl_sync(FULL, pa, 0);
+            pk = __shfl_sync(FULL, pk, 0);
+            if (act) wl[pa + __popc(ba & lt)] = (uint16_t)q;
+            if (valid && !act) U2[pk + __popc(bk & lt)] = (uint16_t)q;
+          }
+          __syncthreads();
+          const int nk = sh[0];
+          nU = sh[1];
+          uint16_t* tmp = U;
+          U = U2;
+          U2 = tmp;
+          if (nk == 0) break;
+          if (tid == 0) cnt.steps++;
+          const int G = pick_group(nk, T);
+          const int groups = T / G, g = tid / G, t = tid & (G - 1);
+          const unsigned gm = G == 32 ? FULL : (((1u << G) - 1u) << (lane & ~(G - 1)));
+          for (int j = g; j < nk; j += groups) {
+            int q = wl[j];
+            visit_coop<SUMS, true>(B, par, m + q, sw, chain, G, t, gm, cnt);
+            if (t == 0) {
+              pri[q] = 0;
+              cnt.visits++;
+            }
+            cnt.busy++;
+          }
+          __syncthreads();
+        }
+      } else {
+        if (tid == 0) {
+          wl[0] = (uint16_t)(nint - 1);
+          sh[2] = 1;
+        }
+        __syncthreads();
+        for (int guard = 0; guard <= nint; guard++) {
+          const int sp = sh[2];
+          if (sp <= 0) break;
+          const int G = pick_group(min(sp, T), T);
+          const int groups = T / G, g = tid / G, t = tid & (G - 1);
+          const unsigned gm = G == 32 ? FULL : (((1u << G) - 1u) << (lane & ~(G - 1)));
+          const int k = min(sp, groups), b0 = sp - k;
+          const int q = g < k ? (int)wl[b0 + g] : 0;
+          __syncthreads();
+          if (tid == 0) {
+            sh[2] = b0;
+            cnt.steps++;
+          }
+          __syncthreads();
+          if (g < k) {
+            visit_coop<SUMS, false>(B, par, m + q, sw, chain, G, t, gm, cnt);
+            if (t == 0) {
+              cnt.visits++;
+              uint32_t cw = B.ch[q];
+              int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+              int n = (l >= m) + (r >= m);
+              if (n) {
+                int pos = atomicAdd(&sh[2], n);
+                if (r >= m) wl[pos++] = (uint16_t)(r - m);
+                if (l >= m) wl[pos] = (uint16_t)(l - m);
+              }
+            }
+            cnt.busy++;
+          }
+          __syncthreads();
+        }
+      }
+      if (a.slice_moves > 0 && (sw + 1) % (uint32_t)a.slice_every == 0) {
+        __syncthreads();
+        slice_step_block(B, a, cz2, sh + 8, nullptr, sw, chain, cnt);
+      }
+      __syncthreads();
+    }
+    if (warp == 0) {
+      EvalOut e = eval_cz(B.cz, nint, B.S, L.nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+      if (lane == 0) {
+        a.out_lc[c] = e.lcost;
+        a.out_sc[c] = e.sc;
+        a.out_ns[c] = e.ns;
+      }
+    }
+    uint32_t* wch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
+    uint32_t* wcz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
+    uint64_t* wS = reinterpret_cast<uint64_t*>(grec + L.off_S);
+    for (int q = tid; q < nint; q += T) {
+      wch[q] = B.ch[q];
+      wcz[q] = B.cz[q];
+    }
+    if (SUMS) {
+      uint64_t* ws = reinterpret_cast<uint64_t*>(grec + L.off_sum);
+      for (int q = tid; q < nint; q += T) ws[q] = B.sum[q];
+    }
+    for (int q = tid; q < L.nw; q += T) wS[q] = B.S[q];
+    __syncthreads();
+  }
+  // every thread: its own proposals/accepts/visits; steps and slice moves counted by one thread/warp
+  unsigned long long v[7] = {cnt.prop, cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc, cnt.busy};
+#pragma unroll
+  for (int q = 0; q < 7; q++) {
+    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(FULL, v[q], o);
+  }
+  if (lane == 0) {
+    // slice moves were counted by all 32 lanes of warp 0
+    v[4] /= 32;
+    v[5] /= 32;
+#pragma unroll
+    for (int q = 0; q < 7; q++)
+      if (v[q]) atomicAdd(&a.stats[q], v[q]);
+  }
+}
+
 // Population resampling: dst chain c <- src chain anc[c] (reference k_copy, :1017-1022).
 __global__ void k_copy(const uint4* __restrict__ src, uint4* __restrict__ dst, const int* __restrict__ anc, int n4) {
   const uint4* s = src + (size_t)anc[blockIdx.x] * n4;
@@ -593,6 +1144,16 @@ static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaSt
   }
 }
 
+template <bool SUMS, int ORDER>
+static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
+  auto k = k_anneal_block<SUMS, ORDER>;
+  size_t smem = BlockSmem::make(a.L, a.slice_moves).total;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<p.grid, 32 * p.warps_per_cta, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, LaunchPlan* plan) {
   int nsm = 0, optin = 0;
   cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
@@ -618,12 +1179,20 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, LaunchPlan* pl
       return cudaSuccess;
     }
   }
-  return cudaErrorNotSupported;
+  // one CTA of 16 warps per chain, label sets in HBM
+  BlockSmem bs = BlockSmem::make(L, 1);
+  if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
+  plan->kind = K_BLOCK;
+  plan->warps_per_cta = 16;
+  plan->grid = nchains;
+  plan->smem = bs.total;
+  return cudaSuccess;
 }
 
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
   if (p.kind == K_WARP) return a.order == 0 ? launch_warp_o<0>(a, p, st) : launch_warp_o<1>(a, p, st);
-  return cudaErrorNotSupported;
+  if (a.L.sums) return a.order == 0 ? launch_block_t<true, 0>(a, p, st) : launch_block_t<true, 1>(a, p, st);
+  return a.order == 0 ? launch_block_t<false, 0>(a, p, st) : launch_block_t<false, 1>(a, p, st);
 }
 
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,

@@ -8,6 +8,7 @@
 //   cz[nint]       u32   cost << 16 | size of node m+i on the sliced network:
 //                        size = |z & ~S|, cost = size + |x & y & ~z & ~S| (x, y: children)
 //   S[nw]          u64   slice set
+//   sum[nint]      u64   (wide layouts) bit c set iff 16-byte chunk c of lab[i] is nonzero
 // Leaf label sets (identical for every chain) are one shared table leaf[m][nw].
 #pragma once
 #include <cuda_runtime.h>
@@ -18,6 +19,8 @@ namespace tsa {
 struct Layout {
   int m, nint, nw;           // leaves, internal nodes, u64 words per label set
   uint32_t off_ch, off_cz, off_S, rec_bytes;
+  int sums;                  // 1: chunk summaries (bit c of a node's u64: 16-byte chunk c nonzero)
+  uint32_t off_sum;          // summaries [nint] u64 inside the record (when sums)
 };
 
 // Everything one sweep launch needs (passed by value).
@@ -33,6 +36,7 @@ struct SweepArgs {
   float sc_target, sc_weight;
   uint32_t key0, key1;
   int slicing, leaf_sc;
+  int exp_device;            // 1: Metropolis with the device expf (reference GPU binary semantics)
   int slice_moves, slice_every, max_slices;
   float* out_lc;             // [nchains] per-chain energy after the launch
   int* out_sc;
@@ -40,6 +44,7 @@ struct SweepArgs {
   unsigned long long* stats; // 9 counters (see tsa_session_stats)
   int* err;                  // nonzero: a bounded wait timed out
   const float* lse_tab;      // 64 floats (device)
+  const uint64_t* leaf_sum;  // [m] chunk summaries of the leaf sets (when L.sums)
 };
 
 // Kernel family chosen by the host for a layout.
