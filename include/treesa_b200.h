@@ -85,7 +85,9 @@ typedef struct tsa_options {
   int32_t exp_mode;           /* Metropolis expf: 0 = the host libm's (bit-exact with the reference's CPU port
                                  csrc/cpu_ref.h, default); 1 = the device's expf (bit-exact with the
                                  reference's GPU binary, csrc/common.h:228 compiled by nvcc) */
-  int32_t reserved[13];
+  int32_t kernel_hint;        /* 0 auto; 1 warp-per-chain kernel (chain in shared memory); 2 CTA-per-chain
+                                 kernel (label sets in HBM).  Never changes a result. */
+  int32_t reserved[12];
 } tsa_options;
 
 /* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the
@@ -142,6 +144,10 @@ void tsa_session_destroy(tsa_session* s);
  * [8] 16-byte label chunks the moves touched; and the summed device time of the sweep kernels. */
 int tsa_session_stats(tsa_session* s, uint64_t* counters9, double* kernel_seconds);
 
+/* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
+ * kernel (1 warp-per-chain, 2 CTA-per-chain), warps per CTA, grid, dynamic shared memory bytes}. */
+int tsa_session_info(tsa_session* s, int32_t* info8);
+
 /* Energies of every chain after the last evaluated level (lcost per slice, sc, |S|), for tests. */
 int tsa_session_energies(tsa_session* s, float* lcost, int32_t* sc, int32_t* ns, char* err, size_t errlen);
 
@@ -160,6 +166,15 @@ int tsa_nccl_unique_id(void* id128, char* err, size_t errlen);
  * No counterpart in the reference (single GPU, csrc/treesa_gpu.cu:1925-1933 copies in place). */
 int tsa_resample_plan(const int* anc, int nloc, int rank, int world, int* src_of, int* send_off, int* send_idx,
                       int* recv_off, int* recv_ids);
+
+/* Self-test of the device's Metropolis arithmetic over the negative floats with bit patterns in
+ * [lo_bits, hi_bits]: checksum = sum over x of (bits(expf'(x)) ^ (bits(x) * 0x9E3779B1)) mod 2^64, where
+ * expf' is the device's host-libm-equivalent expf (correctly rounded Tang evaluation + fix-up table), and
+ * the largest relative error of the single-instruction pre-test 2^(x log2 e) for x >= -17.5.  The host's
+ * libm gives the same checksum iff the device reproduces its expf on every input of the range.
+ * No counterpart in the reference (its GPU binary and its CPU port use different expf). */
+int tsa_expf_selftest(int device, uint32_t lo_bits, uint32_t hi_bits, uint64_t* checksum, double* max_rel_fast,
+                      char* err, size_t errlen);
 
 #ifdef __cplusplus
 }

@@ -51,6 +51,8 @@ def orc():
         L.orc_random_tree.restype = None
         L.orc_labels.argtypes = [C.POINTER(_abi.Instance), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.c_char_p,
                                  C.c_size_t]
+        L.orc_expf_checksum.argtypes = [C.c_uint32, C.c_uint32]
+        L.orc_expf_checksum.restype = C.c_uint64
         L.orc_energy.argtypes = [C.POINTER(_abi.Instance), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
                                  C.POINTER(C.c_float), C.POINTER(C.c_int), C.POINTER(C.c_int),
                                  C.POINTER(C.c_double), C.POINTER(C.c_int), C.c_char_p, C.c_size_t]

@@ -971,4 +971,22 @@ int orc_energy(const tsa_instance* inst, const uint32_t* tree, const uint64_t* S
   return TSA_OK;
 }
 
+// Checksum of the host libm's expf over the float bit patterns [lo, hi] (same formula as the
+// product's tsa_expf_selftest).
+uint64_t orc_expf_checksum(uint32_t lo, uint32_t hi) {
+  uint64_t acc = 0;
+  const long long n = (long long)hi - (long long)lo + 1;
+#pragma omp parallel for reduction(+ : acc) schedule(static)
+  for (long long k = 0; k < n; k++) {
+    uint32_t xb = lo + (uint32_t)k;
+    float x;
+    memcpy(&x, &xb, 4);
+    float g = expf(x);
+    uint32_t gb;
+    memcpy(&gb, &g, 4);
+    acc += (uint64_t)(gb ^ (xb * 0x9E3779B1u));
+  }
+  return acc;
+}
+
 }  // extern "C"

@@ -28,9 +28,9 @@ def _net(rec):
     return engine.Network(rec["ixs"], rec["iy"], rec["nlab"]), O.Net(rec["ixs"], rec["iy"], rec["nlab"])
 
 
-def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None):
+def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None, kernel="auto"):
     opts = dict(betas=betas, niters=niters, nchains=len(trees), sc_target=sc_target, order=order, seed=seed,
-                init_trees=trees)
+                init_trees=trees, kernel_hint=kernel)
     if S is not None:
         opts["init_slices"] = S
     s = engine.Session(net, **opts)
@@ -41,13 +41,20 @@ def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None):
     return t, lab, st
 
 
+WIDE = ["grid24", "grid28", "sq46"]  # 576, 784 and 4140 labels: CTA-per-chain kernel (sq46 with summaries)
+
+
+@pytest.mark.parametrize("kernel", ["warp", "block"])
 @pytest.mark.parametrize("order", ["par", "preorder"])
-@pytest.mark.parametrize("name", SMALL)
-def test_trajectories_bit_exact(name, order):
+@pytest.mark.parametrize("name", SMALL + WIDE)
+def test_trajectories_bit_exact(name, order, kernel):
+    if name in WIDE and kernel == "warp":
+        pytest.skip("wide label sets have no warp-kernel layout")
     rec = _util.instance(name)
     net, onet = _net(rec)
-    trees = _util.start_trees(rec, 64, seed=7)
-    t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 4, order, 7, 24.0)
+    nch = 16 if name in WIDE else 64
+    trees = _util.start_trees(rec, nch, seed=7)
+    t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 4, order, 7, 24.0, kernel=kernel)
     ot, olab, ocnt = O.sweeps(onet, trees, CHECK_BETAS, 4, order=order, seed=7, sc_target=24.0)
     nw = onet.nw
     assert (t == ot).all(), f"{(t != ot).any(1).sum()} chains differ"
@@ -123,3 +130,44 @@ def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
         orc, od = O.run(onet, **kw)
         assert od["tree"] == d["tree"] and od["best_chain"] == d["best_chain"]
         assert abs(od["tc"] - d["tc"]) < 1e-9 and od["sc"] == d["sc"]
+
+
+@pytest.mark.parametrize("kernel", ["warp", "block"])
+@pytest.mark.parametrize("name", ["sat100", "reg3_250", "grid24"])
+def test_fixed_slice_set_bit_exact(name, kernel):
+    """A fixed slice set (labels of size 1): every cost on the sliced network (reference check section C)."""
+    rec = _util.instance(name)
+    if name == "grid24" and kernel == "warp":
+        pytest.skip("wide")
+    net, onet = _net(rec)
+    rng = np.random.default_rng(8)
+    sl = sorted(int(x) for x in rng.choice(rec["nlab"], 8, replace=False))
+    S = np.zeros(onet.nw, np.uint64)
+    for l in sl:
+        S[l >> 6] |= np.uint64(1) << np.uint64(l & 63)
+    trees = _util.start_trees(rec, 32, seed=8)
+    t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 3, "par", 8, 18.0, S=sl, kernel=kernel)
+    ot, olab, ocnt = O.sweeps(onet, trees, CHECK_BETAS, 3, order="par", seed=8, sc_target=18.0,
+                              S=np.tile(S, (32, 1)))
+    assert (t == ot).all() and (lab[:, :, :onet.nw] == olab).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
+
+
+@pytest.mark.parametrize("kernel", ["warp", "block"])
+@pytest.mark.parametrize("name,T", [("sat60", 30), ("reg3_250", 24), ("grid24", 34)])
+def test_slice_moves_match_oracle(name, T, kernel):
+    """Annealed slice sets (reference test (4) configurations).  The slice-move Metropolis test reads float
+    energies (device log2f/exp2f on the GPU, libm on the host); they differ in the last bit at most, which
+    changes a decision with probability ~1e-7 per proposal, so these runs agree exactly."""
+    if name == "grid24" and kernel == "warp":
+        pytest.skip("wide")
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    kw = dict(betas=_util.julia_betas(0.01, 0.5, 8.0), niters=3, nchains=32, sc_target=float(T), slicing=True,
+              seed=5, scheme="indep")
+    rc, d = engine.run(net, kernel_hint=kernel, **kw)
+    orc, od = O.run(onet, **kw)
+    assert rc == 0 and d["valid"] and d["labels_ok"] and d["sc"] <= T
+    assert d["tree"] == od["tree"] and d["sliced"] == od["sliced"] and d["n_repair"] == od["n_repair"]
+    assert d["slice_proposals"] == od["slice_proposals"] and d["slice_accepts"] == od["slice_accepts"]
+    assert abs(d["tc"] - od["tc"]) < 1e-9 and d["sc"] == od["sc"]

@@ -38,7 +38,7 @@ class Options(C.Structure):
                 ("gpu_model", C.POINTER(C.c_double)), ("h100_model", C.POINTER(C.c_double)),
                 ("device", C.c_int32), ("stream", C.c_void_p), ("rank", C.c_int32), ("world_size", C.c_int32),
                 ("nccl_id", C.c_void_p), ("verbose", C.c_int32), ("max_levels", C.c_int32),
-                ("exp_mode", C.c_int32), ("reserved", C.c_int32 * 13)]
+                ("exp_mode", C.c_int32), ("kernel_hint", C.c_int32), ("reserved", C.c_int32 * 12)]
 
 
 class Result(C.Structure):
@@ -62,7 +62,7 @@ TRACE_COLS = ["t", "level", "beta", "best_lcost_per_slice", "best_sc", "mean_E",
 
 EXPORTS = ["tsa_abi_version", "tsa_run", "tsa_result_free", "tsa_session_create", "tsa_session_run",
            "tsa_session_result", "tsa_session_reset", "tsa_session_destroy", "tsa_session_stats",
-           "tsa_session_energies", "tsa_session_chains", "tsa_nccl_unique_id"]
+           "tsa_session_energies", "tsa_session_chains", "tsa_nccl_unique_id", "tsa_session_info"]
 
 
 class Packed:
@@ -97,7 +97,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
                  order="par", seed=1, eval_every=1, slicing=False, slice_moves=1, slice_every=1, max_slices=0,
                  init_slices=(), select_sc=False, init_trees=None, gpu_model=None, h100_model=None, device=0,
                  stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc",
-                 exp_mode="host"):
+                 exp_mode="host", kernel_hint=0):
     o = Options()
     o.betas, _ = keep.arr(np.asarray(betas, np.float32), np.float32, C.c_float)
     o.nbetas = len(betas)
@@ -138,6 +138,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
     o.verbose = int(bool(verbose))
     o.max_levels = int(max_levels)
     o.exp_mode = {"host": 0, "device": 1}[exp_mode]
+    o.kernel_hint = {0: 0, 1: 1, 2: 2, "auto": 0, "warp": 1, "block": 2}[kernel_hint]
     return o
 
 
@@ -196,6 +197,7 @@ def lib():
     L.tsa_session_chains.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.c_char_p,
                                      C.c_size_t]
     L.tsa_nccl_unique_id.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+    L.tsa_session_info.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
     v = L.tsa_abi_version()
     if v != ABI_VERSION:
         raise RuntimeError(f"libtreesa_b200.so ABI version {v}, expected {ABI_VERSION}")

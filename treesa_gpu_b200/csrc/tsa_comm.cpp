@@ -202,7 +202,6 @@ int Comm::allgather_energies(const float* d_lc, const int* d_sc, const int* d_ns
   CCK(cudaMemcpyAsync(glc, p->g_lc, ng * sizeof(float), cudaMemcpyDeviceToHost, st));
   CCK(cudaMemcpyAsync(gsc, p->g_sc, ng * sizeof(int), cudaMemcpyDeviceToHost, st));
   CCK(cudaMemcpyAsync(gns, p->g_ns, ng * sizeof(int), cudaMemcpyDeviceToHost, st));
-  CCK(cudaStreamSynchronize(st));
   return TSA_OK;
 }
 
@@ -213,7 +212,6 @@ int Comm::fetch_record(const uint8_t* d_rec_local, uint32_t bytes, int owner, ui
   NCK(p->N->broadcast(rank == owner ? (const void*)d_rec_local : (const void*)p->recbuf, p->recbuf, bytes, ncclUint8,
                       owner, p->comm, st));
   CCK(cudaMemcpyAsync(host_out, p->recbuf, bytes, cudaMemcpyDeviceToHost, st));
-  CCK(cudaStreamSynchronize(st));
   return TSA_OK;
 }
 

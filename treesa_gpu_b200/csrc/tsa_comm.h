@@ -20,8 +20,10 @@ struct Comm {
   CommImpl* p = nullptr;
   int rank = 0, world = 1;
   ~Comm();
+  // enqueue on st (no synchronization): every chain's energies into host buffers (pinned for overlap)
   int allgather_energies(const float* d_lc, const int* d_sc, const int* d_ns, int nloc, float* glc, int* gsc, int* gns,
                          cudaStream_t st, char* err, size_t errlen);
+  // enqueue on st: the owner's record broadcast to every rank, then copied to host_out
   int fetch_record(const uint8_t* d_rec_local, uint32_t bytes, int owner, uint8_t* host_out, cudaStream_t st,
                    char* err, size_t errlen);
   int resample(const int* anc_global, uint8_t* d_rec, uint8_t* d_rec2, int* d_anc, int nloc, uint32_t rec_bytes,

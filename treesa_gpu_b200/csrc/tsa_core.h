@@ -69,14 +69,10 @@ struct U4 {
 };
 
 TSA_HD void mulhilo(uint32_t a, uint32_t b, uint32_t& hi, uint32_t& lo) {
-#ifdef __CUDA_ARCH__
-  hi = __umulhi(a, b);
-  lo = a * b;
-#else
+  // one 32x32->64 multiply (a single wide IMAD on the device)
   uint64_t p = (uint64_t)a * (uint64_t)b;
   hi = (uint32_t)(p >> 32);
   lo = (uint32_t)p;
-#endif
 }
 
 TSA_HD U4 philox10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0, uint32_t k1) {
@@ -247,12 +243,8 @@ TSA_HD float fixup_lookup(float x, float e, const uint32_t* fx, const uint32_t* 
   return e;
 }
 
-// Metropolis test identical to the host's  u < expf(-beta * dE)  (glibc expf).
-TSA_HD bool metropolis(uint32_t r, float beta, float dE, const double* T, const uint32_t* fx, const uint32_t* fg,
-                       int nfix) {
-  float u = (float)(r >> 8) * (1.0f / 16777216.0f);
-  float x = fmul(-beta, dE);
-  if (!(x < 0.0f)) return true;  // expf(x) >= 1 > u
+// Exact decision u < expf(x) for x < 0 (glibc expf): Tang's correctly rounded value plus the table.
+TSA_HD bool metropolis_exact(float u, float x, const double* T, const uint32_t* fx, const uint32_t* fg, int nfix) {
   float e = tang_expf(x, T);
   // glibc's value differs from e by at most one ulp; only a u next to e can see the difference
   uint32_t eb = f2u(e);
@@ -262,6 +254,37 @@ TSA_HD bool metropolis(uint32_t r, float beta, float dE, const double* T, const 
   if (u >= hi) return false;
   float g = fixup_lookup(x, e, fx, fg, nfix);
   return u < g;
+}
+
+#ifdef __CUDACC__
+// 2^t by the SFU (ex2.approx.f32: relative error about 2^-22 on the whole range)
+__device__ __forceinline__ float ex2_approx(float t) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
+  return y;
+}
+#endif
+
+// Metropolis test identical to the host's  u < expf(-beta * dE)  (glibc expf).  The device first
+// decides with a single-instruction 2^(x log2 e); only when u lies within a relative margin of 8e-6 of
+// that value (6x the worst error of the approximation for -17.5 < x < 0, checked exhaustively on the
+// GPU by tests/test_gpu_metropolis.py) does it evaluate the exact value.  Below x = -17.5, exp(x) is
+// below the smallest nonzero u (2^-24), so only u = 0 can be accepted.
+TSA_HD bool metropolis(uint32_t r, float beta, float dE, const double* T, const uint32_t* fx, const uint32_t* fg,
+                       int nfix) {
+  float u = (float)(r >> 8) * (1.0f / 16777216.0f);
+  float x = fmul(-beta, dE);
+  if (!(x < 0.0f)) return true;  // expf(x) >= 1 > u
+#ifdef __CUDA_ARCH__
+  if (x >= -17.5f) {
+    float ea = ex2_approx(__fmul_rn(x, 1.44269504088896341f));
+    if (u < __fmul_rn(ea, 1.0f - 8e-6f)) return true;
+    if (u > __fmul_rn(ea, 1.0f + 8e-6f)) return false;
+  } else if (r >> 8) {
+    return false;  // u >= 2^-24 > exp(x)
+  }
+#endif
+  return metropolis_exact(u, x, T, fx, fg, nfix);
 }
 
 }  // namespace tsa

@@ -436,6 +436,12 @@ struct tsa_session {
   int *d_sc = nullptr, *d_ns = nullptr, *d_anc = nullptr, *d_err = nullptr;
   unsigned long long* d_stats = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  cudaEvent_t evk[4] = {nullptr, nullptr, nullptr, nullptr};  // kernel start/end, two level parities
+  cudaEvent_t eve[2] = {nullptr, nullptr};                    // energies of a level on the host
+  float* h_lc = nullptr;                                      // pinned [2][nglobal]
+  int *h_sc = nullptr, *h_ns = nullptr;
+  uint8_t* h_best = nullptr;                                  // pinned best record
+  uint8_t* d_cur = nullptr;                                   // buffer holding the current population
   tsa::Comm* comm = nullptr;
   float h_lse[64];
   double t_init = 0;
@@ -468,6 +474,14 @@ struct tsa_session {
     cudaFree(d_stats);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
+    for (auto& e : evk)
+      if (e) cudaEventDestroy(e);
+    for (auto& e : eve)
+      if (e) cudaEventDestroy(e);
+    cudaFreeHost(h_lc);
+    cudaFreeHost(h_sc);
+    cudaFreeHost(h_ns);
+    cudaFreeHost(h_best);
     if (own_stream && st) cudaStreamDestroy(st);
     delete comm;
   }
@@ -496,19 +510,25 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
     CKR(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     s->own_stream = true;
   }
-  if (tsa::plan_sweeps(s->L, s->nchains, s->device, &s->plan) != cudaSuccess) {
+  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, &s->plan) != cudaSuccess) {
     set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
     return TSA_ERR_UNSUPPORTED;
   }
   const size_t recb = (size_t)s->L.rec_bytes * s->nchains;
   CKR(cudaMalloc(&s->d_rec, recb));
   CKR(cudaMalloc(&s->d_init, recb));
-  if (s->scheme != TSA_SCHEME_INDEP) CKR(cudaMalloc(&s->d_rec2, recb));
+  CKR(cudaMalloc(&s->d_rec2, recb));
   CKR(cudaMalloc(&s->d_leaf, s->I.leaf.size() * 8));
   CKR(cudaMalloc(&s->d_lse, 64 * sizeof(float)));
-  CKR(cudaMalloc(&s->d_lc, s->nchains * sizeof(float)));
-  CKR(cudaMalloc(&s->d_sc, s->nchains * sizeof(int)));
-  CKR(cudaMalloc(&s->d_ns, s->nchains * sizeof(int)));
+  CKR(cudaMalloc(&s->d_lc, 2 * s->nchains * sizeof(float)));
+  CKR(cudaMalloc(&s->d_sc, 2 * s->nchains * sizeof(int)));
+  CKR(cudaMalloc(&s->d_ns, 2 * s->nchains * sizeof(int)));
+  CKR(cudaMallocHost(&s->h_lc, 2 * (size_t)s->nglobal * sizeof(float)));
+  CKR(cudaMallocHost(&s->h_sc, 2 * (size_t)s->nglobal * sizeof(int)));
+  CKR(cudaMallocHost(&s->h_ns, 2 * (size_t)s->nglobal * sizeof(int)));
+  CKR(cudaMallocHost(&s->h_best, s->L.rec_bytes));
+  for (auto& e : s->evk) CKR(cudaEventCreate(&e));
+  for (auto& e : s->eve) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   CKR(cudaMalloc(&s->d_anc, s->nchains * sizeof(int)));
   CKR(cudaMalloc(&s->d_err, sizeof(int)));
   CKR(cudaMalloc(&s->d_stats, 9 * sizeof(unsigned long long)));
@@ -642,6 +662,13 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
     delete s;
     return TSA_ERR_ARG;
   }
+  if (O->kernel_hint == 2 && s->I.nw == 1) {  // the CTA-per-chain kernel streams 16-byte chunks
+    Inst& J = s->I;
+    J.nw = 2;
+    J.leaf.assign((size_t)J.m * 2, 0);
+    for (int i = 0; i < J.m; i++)
+      for (int l : J.ixs[i]) J.leaf[(size_t)i * 2 + (l >> 6)] |= 1ull << (l & 63);
+  }
   const Inst& I = s->I;
   s->betas.assign(O->betas, O->betas + O->nbetas);
   if (O->max_levels > 0 && (int)s->betas.size() > O->max_levels) s->betas.resize(O->max_levels);
@@ -724,13 +751,18 @@ int tsa_session_reset(tsa_session* s, char* err, size_t errlen) {
   if (!s) return TSA_ERR_ARG;
   CKR(cudaSetDevice(s->device));
   CKR(cudaMemcpyAsync(s->d_rec, s->d_init, (size_t)s->L.rec_bytes * s->nchains, cudaMemcpyDeviceToDevice, s->st));
+  s->d_cur = s->d_rec;
   int rc = reset_run_state(s, err, errlen);
   if (rc) return rc;
   CKR(cudaStreamSynchronize(s->st));
   return TSA_OK;
 }
 
-// The beta-level loop (run_anneal, csrc/treesa_gpu.cu:1789-1877).
+// The beta-level loop (run_anneal, csrc/treesa_gpu.cu:1789-1877).  Best-of-N runs of the warp kernel are
+// pipelined: level l reads one record buffer and writes the other, its energies go to pinned host memory,
+// and the host scores level l (and, when the best improves, copies the best record out of level l's
+// output buffer) while level l+1 runs; level l+2, which overwrites that buffer, is enqueued after the
+// copy.  Population schemes need level l's energies before level l+1 and run level by level.
 int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   if (!s) return TSA_ERR_ARG;
   if (s->ran) {
@@ -740,16 +772,16 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   CKR(cudaSetDevice(s->device));
   const int nch = s->nchains, ng = s->nglobal;
   const size_t nlev = s->betas.size();
+  const uint32_t rb = s->L.rec_bytes;
   double t0 = now_s();
   s->lc.assign(nch, 0.f);
   s->sc.assign(nch, 0);
   s->ns.assign(nch, 0);
-  std::vector<float> glc(ng);
-  std::vector<int> gsc(ng), gns(ng);
   std::vector<int> family(ng), nfam(ng);
   std::iota(family.begin(), family.end(), 0);
   std::mt19937_64 hrng(splitmix64(s->seed + 777));
   float beta_last = s->betas[0];
+  const bool pipelined = s->scheme == TSA_SCHEME_INDEP && s->plan.kind == tsa::K_WARP;
   tsa::SweepArgs a{};
   a.L = s->L;
   a.leaf = s->d_leaf;
@@ -767,57 +799,13 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.slice_moves = s->slice_moves;
   a.slice_every = s->slice_every;
   a.max_slices = s->max_slices;
-  a.out_lc = s->d_lc;
-  a.out_sc = s->d_sc;
-  a.out_ns = s->d_ns;
   a.stats = s->d_stats;
   a.err = s->d_err;
   a.lse_tab = s->d_lse;
   a.leaf_sum = s->d_leaf_sum;
-  for (size_t lev = 0; lev < nlev; lev++) {
-    a.recs = s->d_rec;
-    a.beta = s->betas[lev];
-    a.sweep0 = s->sweep_ctr;
-    CKR(cudaEventRecord(s->ev0, s->st));
-    CKR(tsa::launch_sweeps(a, s->plan, s->st));
-    CKR(cudaEventRecord(s->ev1, s->st));
-    s->launches++;
-    s->sweep_ctr += (uint32_t)s->niters;
-    const bool last = lev + 1 == nlev;
-    const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || last;
-    if (!eval) {
-      CKR(cudaEventSynchronize(s->ev1));
-      float ms = 0;
-      CKR(cudaEventElapsedTime(&ms, s->ev0, s->ev1));
-      s->kernel_ms += ms;
-      continue;
-    }
-    CKR(cudaMemcpyAsync(s->lc.data(), s->d_lc, nch * sizeof(float), cudaMemcpyDeviceToHost, s->st));
-    CKR(cudaMemcpyAsync(s->sc.data(), s->d_sc, nch * sizeof(int), cudaMemcpyDeviceToHost, s->st));
-    CKR(cudaMemcpyAsync(s->ns.data(), s->d_ns, nch * sizeof(int), cudaMemcpyDeviceToHost, s->st));
-    CKR(cudaStreamSynchronize(s->st));
-    s->d2h += (size_t)nch * (sizeof(float) + 2 * sizeof(int));
-    {
-      float ms = 0;
-      CKR(cudaEventElapsedTime(&ms, s->ev0, s->ev1));
-      s->kernel_ms += ms;
-    }
-    int herr = 0;
-    CKR(cudaMemcpy(&herr, s->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (herr) {
-      set_err(err, errlen, "a bounded device wait timed out (code %d)", herr);
-      return TSA_ERR_TIMEOUT;
-    }
-    // the whole population's energies (all ranks)
-    if (s->world > 1) {
-      int rc = s->comm->allgather_energies(s->d_lc, s->d_sc, s->d_ns, nch, glc.data(), gsc.data(), gns.data(), s->st,
-                                           err, errlen);
-      if (rc) return rc;
-    } else {
-      std::copy(s->lc.begin(), s->lc.end(), glc.begin());
-      std::copy(s->sc.begin(), s->sc.end(), gsc.begin());
-      std::copy(s->ns.begin(), s->ns.end(), gns.begin());
-    }
+  s->best.resize(rb);
+  // host side of one evaluated level: best tracking, trace, population step (returns the ancestors)
+  auto process = [&](size_t lev, const float* glc, const int* gsc, const int* gns, int* improved) {
     int bi = 0;
     double bs = INFINITY, meanE = 0, meanNs = 0;
     for (int c = 0; c < ng; c++) {
@@ -831,22 +819,12 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     }
     meanE /= ng;
     meanNs /= ng;
+    *improved = -1;
     if (bs < s->best_score) {
       s->best_score = bs;
       s->best_chain = bi;
       s->best_level = (int)lev;
-      s->best.resize(s->L.rec_bytes);
-      int owner = bi / nch;
-      if (s->world > 1) {
-        int rc = s->comm->fetch_record(s->d_rec + (size_t)(bi % nch) * s->L.rec_bytes, s->L.rec_bytes, owner,
-                                       s->best.data(), s->st, err, errlen);
-        if (rc) return rc;
-      } else {
-        CKR(cudaMemcpyAsync(s->best.data(), s->d_rec + (size_t)bi * s->L.rec_bytes, s->L.rec_bytes,
-                            cudaMemcpyDeviceToHost, s->st));
-        s->d2h += s->L.rec_bytes;
-        CKR(cudaStreamSynchronize(s->st));
-      }
+      *improved = bi;
     }
     std::fill(nfam.begin(), nfam.end(), 0);
     int nf = 0;
@@ -855,60 +833,197 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     double row[10] = {now_s() - t0, (double)lev, (double)s->betas[lev], (double)glc[bi], (double)gsc[bi], meanE,
                       (double)nf, 0.0, (double)gns[bi], meanNs};
     s->trace.insert(s->trace.end(), row, row + 10);
-    if (s->verbose && (lev % 25 == 0 || last))
+    if (s->verbose && (lev % 25 == 0 || lev + 1 == nlev))
       fprintf(stderr, "lev %4zu beta %7.3f  best(l2cost/slice %.3f sc %d |S| %d)  meanE %.3f  families %d  t=%.2fs\n",
               lev, s->betas[lev], (double)glc[bi], gsc[bi], gns[bi], meanE, nf, now_s() - t0);
-    if (last || s->scheme == TSA_SCHEME_INDEP) continue;
-    std::vector<int> anc(ng);
-    if (s->scheme == TSA_SCHEME_PA) {  // :1837-1856
-      double db = s->betas[lev + 1] - beta_last;
-      beta_last = s->betas[lev + 1];
-      std::vector<double> w(ng);
-      double Emin = INFINITY;
-      for (int c = 0; c < ng; c++) Emin = std::min(Emin, s->energyE(glc[c], gsc[c], gns[c]));
-      double wsum = 0;
-      for (int c = 0; c < ng; c++) {
-        w[c] = exp(-db * (s->energyE(glc[c], gsc[c], gns[c]) - Emin));
-        wsum += w[c];
-      }
-      double u = std::uniform_real_distribution<double>(0, 1)(hrng), acc = 0;
-      int j = 0;
-      for (int c = 0; c < ng; c++) {
-        acc += w[c] / wsum * ng;
-        while (j < ng && j + u < acc) anc[j++] = c;
-      }
-      while (j < ng) anc[j++] = ng - 1;
-    } else {  // truncation, :1857-1869
-      std::vector<int> idx(ng);
-      std::iota(idx.begin(), idx.end(), 0);
-      std::sort(idx.begin(), idx.end(), [&](int x, int y) {
-        return s->energyE(glc[x], gsc[x], gns[x]) < s->energyE(glc[y], gsc[y], gns[y]);
-      });
-      std::iota(anc.begin(), anc.end(), 0);
-      int nrep = (int)(s->trunc_frac * ng);
-      for (int q = 0; q < nrep; q++) anc[idx[ng - 1 - q]] = idx[q];
+  };
+  // enqueue: energies of this level (all ranks) into pinned host slot q
+  auto gather = [&](int q) -> int {
+    if (s->world > 1)
+      return s->comm->allgather_energies(s->d_lc + (size_t)q * nch, s->d_sc + (size_t)q * nch,
+                                         s->d_ns + (size_t)q * nch, nch, s->h_lc + (size_t)q * ng,
+                                         s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, s->st, err, errlen);
+    CKR(cudaMemcpyAsync(s->h_lc + (size_t)q * ng, s->d_lc + (size_t)q * nch, nch * sizeof(float),
+                        cudaMemcpyDeviceToHost, s->st));
+    CKR(cudaMemcpyAsync(s->h_sc + (size_t)q * ng, s->d_sc + (size_t)q * nch, nch * sizeof(int),
+                        cudaMemcpyDeviceToHost, s->st));
+    CKR(cudaMemcpyAsync(s->h_ns + (size_t)q * ng, s->d_ns + (size_t)q * nch, nch * sizeof(int),
+                        cudaMemcpyDeviceToHost, s->st));
+    return TSA_OK;
+  };
+  // enqueue: copy global chain g's record out of buffer buf into the pinned best record
+  auto fetch_best = [&](int g, uint8_t* buf) -> int {
+    s->d2h += rb;
+    if (s->world > 1)
+      return s->comm->fetch_record(buf + (size_t)(g % nch) * rb, rb, g / nch, s->h_best, s->st, err, errlen);
+    CKR(cudaMemcpyAsync(s->h_best, buf + (size_t)g * rb, rb, cudaMemcpyDeviceToHost, s->st));
+    return TSA_OK;
+  };
+  auto check_err = [&]() -> int {
+    int herr = 0;
+    CKR(cudaMemcpy(&herr, s->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) {
+      set_err(err, errlen, "a bounded device wait timed out (code %d)", herr);
+      return TSA_ERR_TIMEOUT;
     }
-    if (s->world > 1) {
-      int rc = s->comm->resample(anc.data(), s->d_rec, s->d_rec2, s->d_anc, nch, s->L.rec_bytes, s->st, err, errlen);
-      if (rc) return rc;
-    } else {
-      CKR(cudaMemcpyAsync(s->d_anc, anc.data(), nch * sizeof(int), cudaMemcpyHostToDevice, s->st));
-      s->h2d += nch * sizeof(int);
-      CKR(tsa::launch_copy_chains(s->d_rec, s->d_rec2, s->d_anc, nch, s->L.rec_bytes, s->st));
+    return TSA_OK;
+  };
+  int rc = TSA_OK;
+  uint8_t* buf[2] = {s->d_rec, s->d_rec2};
+  if (pipelined) {
+    long pend = -1;  // evaluated level whose energies are in flight
+    for (size_t lev = 0; lev <= nlev && rc == TSA_OK; lev++) {
+      if (lev < nlev) {
+        const int q = (int)(lev & 1);
+        if (lev >= 2) {  // the timing events of level lev-2 are reused now
+          CKR(cudaEventSynchronize(s->evk[2 * q + 1]));
+          float ms = 0;
+          CKR(cudaEventElapsedTime(&ms, s->evk[2 * q], s->evk[2 * q + 1]));
+          s->kernel_ms += ms;
+        }
+        a.recs = buf[q];
+        a.recs_out = buf[q ^ 1];
+        a.beta = s->betas[lev];
+        a.sweep0 = s->sweep_ctr;
+        a.out_lc = s->d_lc + (size_t)q * nch;
+        a.out_sc = s->d_sc + (size_t)q * nch;
+        a.out_ns = s->d_ns + (size_t)q * nch;
+        CKR(cudaEventRecord(s->evk[2 * q], s->st));
+        CKR(tsa::launch_sweeps(a, s->plan, s->st));
+        CKR(cudaEventRecord(s->evk[2 * q + 1], s->st));
+        s->launches++;
+        s->sweep_ctr += (uint32_t)s->niters;
+      }
+      if (pend >= 0) {
+        const int q = (int)(pend & 1);
+        CKR(cudaEventSynchronize(s->eve[q]));
+        int improved;
+        process((size_t)pend, s->h_lc + (size_t)q * ng, s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, &improved);
+        if (improved >= 0) rc = fetch_best(improved, buf[q ^ 1]);  // level pend's output buffer
+        pend = -1;
+      }
+      if (lev < nlev && rc == TSA_OK) {
+        const int q = (int)(lev & 1);
+        const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || lev + 1 == nlev;
+        if (eval) {
+          rc = gather(q);
+          if (rc == TSA_OK) {
+            CKR(cudaEventRecord(s->eve[q], s->st));
+            s->d2h += (size_t)nch * 12;
+            pend = (long)lev;
+          }
+        }
+      }
     }
-    std::swap(s->d_rec, s->d_rec2);
-    std::vector<int> nfm(ng);
-    for (int c = 0; c < ng; c++) nfm[c] = family[anc[c]];
-    family.swap(nfm);
-    s->nresample++;
+    for (size_t lev = nlev >= 2 ? nlev - 2 : 0; lev < nlev && rc == TSA_OK; lev++) {  // the last two levels
+      const int q = (int)(lev & 1);
+      CKR(cudaEventSynchronize(s->evk[2 * q + 1]));
+      float ms = 0;
+      CKR(cudaEventElapsedTime(&ms, s->evk[2 * q], s->evk[2 * q + 1]));
+      s->kernel_ms += ms;
+    }
+    s->d_cur = buf[nlev & 1];
+  } else {
+    s->d_cur = s->d_rec;
+    for (size_t lev = 0; lev < nlev && rc == TSA_OK; lev++) {
+      a.recs = s->d_cur;
+      a.recs_out = s->d_cur;
+      a.beta = s->betas[lev];
+      a.sweep0 = s->sweep_ctr;
+      a.out_lc = s->d_lc;
+      a.out_sc = s->d_sc;
+      a.out_ns = s->d_ns;
+      CKR(cudaEventRecord(s->evk[0], s->st));
+      CKR(tsa::launch_sweeps(a, s->plan, s->st));
+      CKR(cudaEventRecord(s->evk[1], s->st));
+      s->launches++;
+      s->sweep_ctr += (uint32_t)s->niters;
+      const bool last = lev + 1 == nlev;
+      const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || last;
+      if (eval) {
+        rc = gather(0);
+        if (rc) break;
+        s->d2h += (size_t)nch * 12;
+      }
+      CKR(cudaStreamSynchronize(s->st));
+      float ms = 0;
+      CKR(cudaEventElapsedTime(&ms, s->evk[0], s->evk[1]));
+      s->kernel_ms += ms;
+      if ((rc = check_err())) break;
+      if (!eval) continue;
+      const float* glc = s->h_lc;
+      const int *gsc = s->h_sc, *gns = s->h_ns;
+      int improved;
+      process(lev, glc, gsc, gns, &improved);
+      if (improved >= 0) {
+        if ((rc = fetch_best(improved, s->d_cur))) break;
+        CKR(cudaStreamSynchronize(s->st));
+      }
+      if (last || s->scheme == TSA_SCHEME_INDEP) continue;
+      std::vector<int> anc(ng);
+      if (s->scheme == TSA_SCHEME_PA) {  // :1837-1856
+        double db = s->betas[lev + 1] - beta_last;
+        beta_last = s->betas[lev + 1];
+        std::vector<double> w(ng);
+        double Emin = INFINITY;
+        for (int c = 0; c < ng; c++) Emin = std::min(Emin, s->energyE(glc[c], gsc[c], gns[c]));
+        double wsum = 0;
+        for (int c = 0; c < ng; c++) {
+          w[c] = exp(-db * (s->energyE(glc[c], gsc[c], gns[c]) - Emin));
+          wsum += w[c];
+        }
+        double u = std::uniform_real_distribution<double>(0, 1)(hrng), acc = 0;
+        int j = 0;
+        for (int c = 0; c < ng; c++) {
+          acc += w[c] / wsum * ng;
+          while (j < ng && j + u < acc) anc[j++] = c;
+        }
+        while (j < ng) anc[j++] = ng - 1;
+      } else {  // truncation, :1857-1869
+        std::vector<int> idx(ng);
+        std::iota(idx.begin(), idx.end(), 0);
+        std::sort(idx.begin(), idx.end(), [&](int x, int y) {
+          return s->energyE(glc[x], gsc[x], gns[x]) < s->energyE(glc[y], gsc[y], gns[y]);
+        });
+        std::iota(anc.begin(), anc.end(), 0);
+        int nrep = (int)(s->trunc_frac * ng);
+        for (int q = 0; q < nrep; q++) anc[idx[ng - 1 - q]] = idx[q];
+      }
+      uint8_t* other = s->d_cur == s->d_rec ? s->d_rec2 : s->d_rec;
+      if (s->world > 1) {
+        rc = s->comm->resample(anc.data(), s->d_cur, other, s->d_anc, nch, rb, s->st, err, errlen);
+        if (rc) break;
+      } else {
+        CKR(cudaMemcpyAsync(s->d_anc, anc.data(), nch * sizeof(int), cudaMemcpyHostToDevice, s->st));
+        s->h2d += nch * sizeof(int);
+        CKR(tsa::launch_copy_chains(s->d_cur, other, s->d_anc, nch, rb, s->st));
+      }
+      s->d_cur = other;
+      std::vector<int> nfm(ng);
+      for (int c = 0; c < ng; c++) nfm[c] = family[anc[c]];
+      family.swap(nfm);
+      s->nresample++;
+    }
   }
+  if (rc) return rc;
   CKR(cudaStreamSynchronize(s->st));
+  if ((rc = check_err())) return rc;
+  memcpy(s->best.data(), s->h_best, rb);
+  // the energies of the last level, this rank's chains
+  {
+    const int q = pipelined ? (int)((nlev - 1) & 1) : 0;
+    const size_t off = (size_t)q * ng + (size_t)s->rank * nch;
+    memcpy(s->lc.data(), s->h_lc + off, nch * sizeof(float));
+    memcpy(s->sc.data(), s->h_sc + off, nch * sizeof(int));
+    memcpy(s->ns.data(), s->h_ns + off, nch * sizeof(int));
+  }
   unsigned long long st[9];
   CKR(cudaMemcpy(st, s->d_stats, sizeof st, cudaMemcpyDeviceToHost));
+  s->d2h += sizeof st;
   for (int q = 0; q < 9; q++) s->stats[q] = st[q];
   s->stats[7] = s->launches;
   if (s->world > 1) {
-    int rc = s->comm->sum_u64(s->stats, 7, s->st, err, errlen);
+    rc = s->comm->sum_u64(s->stats, 7, s->st, err, errlen);
     if (rc) return rc;
   }
   s->t_anneal = now_s() - t0;
@@ -1019,6 +1134,19 @@ int tsa_session_stats(tsa_session* s, uint64_t* c9, double* ksec) {
   return TSA_OK;
 }
 
+int tsa_session_info(tsa_session* s, int32_t* v) {
+  if (!s || !v) return TSA_ERR_ARG;
+  v[0] = s->L.m;
+  v[1] = s->L.nint;
+  v[2] = s->L.nw;
+  v[3] = (int32_t)s->L.rec_bytes;
+  v[4] = s->plan.kind == tsa::K_WARP ? 1 : 2;
+  v[5] = s->plan.warps_per_cta;
+  v[6] = s->plan.grid;
+  v[7] = (int32_t)s->plan.smem;
+  return TSA_OK;
+}
+
 int tsa_session_energies(tsa_session* s, float* lcost, int32_t* sc, int32_t* ns, char* err, size_t errlen) {
   if (!s) return TSA_ERR_ARG;
   if ((int)s->lc.size() != s->nchains) {
@@ -1036,7 +1164,7 @@ int tsa_session_chains(tsa_session* s, uint32_t* trees, uint64_t* labels, char* 
   CKR(cudaSetDevice(s->device));
   const Layout& L = s->L;
   std::vector<uint8_t> host((size_t)L.rec_bytes * s->nchains);
-  CKR(cudaMemcpyAsync(host.data(), s->d_rec, host.size(), cudaMemcpyDeviceToHost, s->st));
+  CKR(cudaMemcpyAsync(host.data(), s->d_cur ? s->d_cur : s->d_rec, host.size(), cudaMemcpyDeviceToHost, s->st));
   CKR(cudaStreamSynchronize(s->st));
   for (int c = 0; c < s->nchains; c++) {
     const uint8_t* rec = &host[(size_t)c * L.rec_bytes];
@@ -1047,5 +1175,33 @@ int tsa_session_chains(tsa_session* s, uint32_t* trees, uint64_t* labels, char* 
 }
 
 int tsa_nccl_unique_id(void* id128, char* err, size_t errlen) { return tsa::comm_unique_id(id128, err, errlen); }
+
+int tsa_expf_selftest(int device, uint32_t lo_bits, uint32_t hi_bits, uint64_t* checksum, double* max_rel_fast,
+                      char* err, size_t errlen) {
+  if (lo_bits < 0x80000000u || hi_bits < lo_bits) {
+    set_err(err, errlen, "range must be negative floats with lo <= hi");
+    return TSA_ERR_ARG;
+  }
+  CKR(cudaSetDevice(device));
+  unsigned long long* d_sum = nullptr;
+  unsigned int* d_err = nullptr;
+  CKR(cudaMalloc(&d_sum, sizeof *d_sum));
+  CKR(cudaMalloc(&d_err, sizeof *d_err));
+  CKR(cudaMemset(d_sum, 0, sizeof *d_sum));
+  CKR(cudaMemset(d_err, 0, sizeof *d_err));
+  cudaError_t e = tsa::expf_selftest(lo_bits, hi_bits, d_sum, d_err, 0);
+  unsigned long long hsum = 0;
+  unsigned int herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&hsum, d_sum, sizeof hsum, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(&herr, d_err, sizeof herr, cudaMemcpyDeviceToHost);
+  cudaFree(d_sum);
+  cudaFree(d_err);
+  CKR(e);
+  float f;
+  memcpy(&f, &herr, 4);
+  if (checksum) *checksum = hsum;
+  if (max_rel_fast) *max_rel_fast = f;
+  return TSA_OK;
+}
 
 }  // extern "C"

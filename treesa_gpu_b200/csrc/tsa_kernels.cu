@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   uint16_t* wl = par + W.nint2;
   uint16_t* U = wl + W.nint2;
   uint32_t* cz2 = reinterpret_cast<uint32_t*>(slot + W.off_scr);
-  const int m = L.m, nint = L.nint;
+  const int m = L.m, nint = L.nint, nint2 = W.nint2;
   const unsigned FULL = 0xFFFFFFFFu;
   const unsigned lt = (1u << lane) - 1u;
   Counters cnt{};
@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
         int nU = nint;
         __syncwarp();
         for (int guard = 0; guard <= nint; guard++) {
-          int nk = 0, nu = 0;
+          int nk = 0, nu = 0, nc = 0;
           for (int base = 0; base < nU; base += 32) {
             int j = base + lane;
             bool valid = j < nU;
@@ -495,17 +495,27 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
                 if (pr && ((pr << 16) | (uint32_t)r) > key) act = false;
               }
             }
-            unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
+            // active nodes whose children are both leaves make no proposal: they only become visited
+            bool cher = act && (int)(ch[i] & 0xFFFFu) < m && (int)(ch[i] >> 16) < m;
+            bool prop = act && !cher;
+            unsigned ba = __ballot_sync(FULL, prop), bc = __ballot_sync(FULL, cher),
+                     bk = __ballot_sync(FULL, valid && !act);
             __syncwarp();
-            if (act) wl[nk + __popc(ba & lt)] = (uint16_t)i;
+            if (prop) wl[nk + __popc(ba & lt)] = (uint16_t)i;
+            if (cher) wl[nint2 - 1 - (nc + __popc(bc & lt))] = (uint16_t)i;
             if (valid && !act) U[nu + __popc(bk & lt)] = (uint16_t)i;
             nk += __popc(ba);
+            nc += __popc(bc);
             nu += __popc(bk);
           }
           nU = nu;
-          if (nk == 0) break;
+          if (nk + nc == 0) break;
           cnt.steps++;
           __syncwarp();
+          for (int j = lane; j < nc; j += 32) {
+            pri[wl[nint2 - 1 - j]] = 0;
+            cnt.visits++;
+          }
           for (int j = lane; j < nk; j += 32) {
             int i = wl[j];
             visit<NW, true>(X_, lab, ch, cz, S, par, m + i, sw, chain, cnt);
@@ -526,8 +536,23 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
           __syncwarp();
           uint32_t cw = 0;
           if (lane < k) cw = visit<NW, false>(X_, lab, ch, cz, S, par, v, sw, chain, cnt);
+          // internal children with two leaf children are visited here and now (an empty visit)
           bool c1 = lane < k && (int)(cw & 0xFFFFu) >= m;
           bool c2 = lane < k && (int)(cw >> 16) >= m;
+          if (c1) {
+            uint32_t g = ch[(cw & 0xFFFFu) - m];
+            if ((int)(g & 0xFFFFu) < m && (int)(g >> 16) < m) {
+              c1 = false;
+              cnt.visits++;
+            }
+          }
+          if (c2) {
+            uint32_t g = ch[(cw >> 16) - m];
+            if ((int)(g & 0xFFFFu) < m && (int)(g >> 16) < m) {
+              c2 = false;
+              cnt.visits++;
+            }
+          }
           unsigned b1 = __ballot_sync(FULL, c1), b2 = __ballot_sync(FULL, c2);
           int pos = b0 + __popc(b1 & lt) + __popc(b2 & lt);
           if (c2) wl[pos++] = (uint16_t)((cw >> 16) - (uint32_t)m);
@@ -555,7 +580,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
     __syncwarp();
     if (lane == 0) {
       fence_proxy_async();
-      bulk_s2g(grec, slot, L.rec_bytes);
+      bulk_s2g(a.recs_out + (size_t)c * L.rec_bytes, slot, L.rec_bytes);
       bulk_wait_read();
     }
     __syncwarp();
@@ -1154,13 +1179,13 @@ static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaS
   return cudaGetLastError();
 }
 
-cudaError_t plan_sweeps(const Layout& L, int nchains, int device, LaunchPlan* plan) {
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, LaunchPlan* plan) {
   int nsm = 0, optin = 0;
   cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   if (e != cudaSuccess) return e;
-  bool warp_ok = (L.nw == 1 || L.nw == 2 || L.nw == 4 || L.nw == 6 || L.nw == 8);
+  bool warp_ok = (L.nw == 1 || L.nw == 2 || L.nw == 4 || L.nw == 6 || L.nw == 8) && hint != 2;
   if (warp_ok) {
     // as many chain slots per CTA as fit (at most 16 warps), one CTA per SM
     int wpc = 16;
@@ -1180,6 +1205,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, LaunchPlan* pl
     }
   }
   // one CTA of 16 warps per chain, label sets in HBM
+  if (hint == 1) return cudaErrorNotSupported;
   BlockSmem bs = BlockSmem::make(L, 1);
   if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
   plan->kind = K_BLOCK;
@@ -1210,5 +1236,44 @@ cudaError_t upload_lse_table(const float* host64, float* dev64, cudaStream_t st)
 }
 
 int fixup_count() { return kExpfFixN; }
+
+// Self-test of the Metropolis arithmetic over the float bit patterns [lo, hi] (all negative):
+// checksum of the device's host-libm-equivalent expf (Tang + fix-up table) and the largest relative
+// error of the ex2.approx pre-test against the correctly rounded value for x >= -17.5.
+__global__ void k_expf_selftest(uint32_t lo, uint32_t hi, unsigned long long* sum, unsigned int* maxerr_bits) {
+  __shared__ double T[64];
+  for (int q = threadIdx.x; q < 64; q += blockDim.x) T[q] = c_exp_tab[q];
+  __syncthreads();
+  unsigned long long acc = 0;
+  float worst = 0.f;
+  const uint64_t n = (uint64_t)hi - lo + 1;
+  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (uint64_t)gridDim.x * blockDim.x) {
+    uint32_t xb = lo + (uint32_t)k;
+    float x = __uint_as_float(xb);
+    float e = tang_expf(x, T);
+    float g = fixup_lookup(x, e, kExpfFixX, kExpfFixG, kExpfFixN);
+    acc += (unsigned long long)(__float_as_uint(g) ^ (xb * 0x9E3779B1u));
+    if (x >= -17.5f && e > 0.f) {
+      float ea = ex2_approx(__fmul_rn(x, 1.44269504088896341f));
+      float rel = fabsf(ea - e) / e;
+      worst = fmaxf(worst, rel);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    worst = fmaxf(worst, __shfl_xor_sync(0xFFFFFFFFu, worst, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(sum, acc);
+    atomicMax(maxerr_bits, __float_as_uint(worst));
+  }
+}
+
+cudaError_t expf_selftest(uint32_t lo, uint32_t hi, unsigned long long* d_sum, unsigned int* d_err, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyToSymbolAsync(c_exp_tab, kExp2Tab64, sizeof(kExp2Tab64), 0, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return e;
+  k_expf_selftest<<<148 * 8, 256, 0, st>>>(lo, hi, d_sum, d_err);
+  return cudaGetLastError();
+}
 
 }  // namespace tsa

@@ -26,7 +26,8 @@ struct Layout {
 // Everything one sweep launch needs (passed by value).
 struct SweepArgs {
   Layout L;
-  uint8_t* recs;             // [nchains] records of rec_bytes
+  uint8_t* recs;             // [nchains] records of rec_bytes (input)
+  uint8_t* recs_out;         // where the warp kernel writes the records back (may equal recs)
   const uint64_t* leaf;      // [m][nw]
   int nchains, chain0;       // local chain count, global id of local chain 0
   int order;                 // 0 par, 1 preorder
@@ -58,11 +59,12 @@ struct LaunchPlan {
 };
 
 // Host-side entry points (tsa_kernels.cu).
-cudaError_t plan_sweeps(const Layout& L, int nchains, int device, LaunchPlan* plan);
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, LaunchPlan* plan);
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
                                cudaStream_t st);
 cudaError_t upload_lse_table(const float* host64, float* dev64, cudaStream_t st);
 int fixup_count();
+cudaError_t expf_selftest(uint32_t lo, uint32_t hi, unsigned long long* d_sum, unsigned int* d_err, cudaStream_t st);
 
 }  // namespace tsa

@@ -105,10 +105,16 @@ class Session:
                    what="tsa_session_energies")
         return lc, sc, ns
 
+    def info(self):
+        v = (C.c_int32 * 8)()
+        self.L.tsa_session_info(self.h, v)
+        keys = ["m", "nint", "nw", "rec_bytes", "kernel", "warps_per_cta", "grid", "smem"]
+        return dict(zip(keys, [int(x) for x in v]))
+
     def chains(self):
         nint = self.net.m - 1
         t = np.zeros((self.nchains, nint), np.uint32)
-        lab = np.zeros((self.nchains, nint, self.net.nw), np.uint64)
+        lab = np.zeros((self.nchains, nint, self.info()["nw"]), np.uint64)
         self._call(self.L.tsa_session_chains, t.ctypes.data_as(C.POINTER(C.c_uint32)),
                    lab.ctypes.data_as(C.POINTER(C.c_uint64)), what="tsa_session_chains")
         return t, lab
