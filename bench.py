@@ -32,25 +32,66 @@ METRIC = "node visits/s"
 UNIT = "visits/s"
 
 
-def workload(nchains):
-    from tests import _util
-    rec = _util.instance("sat100")
-    return dict(rec=rec, nchains=nchains, betas=_util.julia_betas(0.01, 0.05, 15.0), niters=10, sc_target=20.0,
-                order="par", scheme="indep", seed=1)
+CONFIGS = {
+    "c1": "C1: random 3-SAT n=60 m=256 (sat60), path start in clause order, order preorder, sc_target 20, "
+          "64 chains, betas 0.01:0.05:15 x 10 sweeps",
+    "c2": "C2: random 3-SAT n=100 m=426 (sat100), spectral start, order par, tc/sc sc_target 20, best-of-N, "
+          "{n} chains per GPU, betas 0.01:0.05:15 x 10 sweeps",
+    "c3": "C3: random 3-regular n=2000 (configuration model, seed 1), 3000 edge + 2000 vertex tensors, "
+          "spectral start, order par, population annealing (resampling every beta), {n} chains per GPU, "
+          "betas 0.01:0.05:15 x 10 sweeps",
+    "c4": "C4: 64x64 open lattice (4096 tensors, 8064 labels), row-major path start, order par, best-of-N, "
+          "{n} chains per GPU x 20 sweeps, betas 0.01:0.05:15",
+    "c5": "C5: grid 3-SAT L=24 alpha 4.26 (2454 clauses, 576 vars, seed 1), slicing sc_target 30, greedy start, "
+          "truncation selection, {n} chains per GPU, betas 0.01:0.05:15 x 10 sweeps",
+}
+DEFAULT_CHAINS = {"c1": 64, "c2": 4096, "c3": 1024, "c4": 72, "c5": 576}
+
+
+def workload(nchains, config="c2"):
+    """The BASELINE configuration as (instance, schedule, options); start trees built by start_trees."""
+    from tests import _instances, _util
+    betas = _util.julia_betas(0.01, 0.05, 15.0)
+    base = dict(config=config, nchains=nchains, betas=betas, niters=10, sc_target=20.0, order="par",
+                scheme="indep", seed=1, slicing=False)
+    if config in ("c1", "c2"):
+        rec = _util.instance("sat60" if config == "c1" else "sat100")
+        base.update(rec=rec)
+        if config == "c1":
+            base.update(order="preorder")
+    else:
+        ixs, iy = {"c3": lambda: _instances.reg3_dual(2000, 1), "c4": lambda: _instances.sq(64),
+                   "c5": lambda: _instances.grid_ksat(24, 4.26, 1)}[config]()
+        labs = {l for ix in ixs for l in ix}
+        base.update(rec=dict(ixs=ixs, iy=iy, m=len(ixs), nlab=1 + max(labs)))
+        if config == "c3":
+            base.update(scheme="pa")
+        elif config == "c4":
+            base.update(niters=20)
+        else:
+            base.update(scheme="trunc", slicing=True, sc_target=30.0)
+    return base
 
 
 def config_dict(W, world):
-    return {"workload": "C2: random 3-SAT n=100 m=426 (sat100), spectral start, order par, tc/sc sc_target 20, "
-                        f"best-of-N, {W['nchains']} chains per GPU, betas 0.01:0.05:15 x {W['niters']} sweeps",
-            "instance": "sat100", "m": W["rec"]["m"], "labels": W["rec"]["nlab"], "chains_per_gpu": W["nchains"],
-            "levels": len(W["betas"]), "sweeps_per_level": W["niters"], "parallelism": f"chains sharded over {world} GPU(s)",
-            "l2": "flushed between steps (256 MiB write; population 42 MB is below L2)"}
+    return {"workload": CONFIGS[W["config"]].format(n=W["nchains"]), "config": W["config"],
+            "m": W["rec"]["m"], "labels": W["rec"]["nlab"], "chains_per_gpu": W["nchains"],
+            "levels": len(W["betas"]), "sweeps_per_level": W["niters"],
+            "parallelism": f"chains sharded over {world} GPU(s)",
+            "l2": "flushed between steps (256 MiB write)"}
 
 
-def start_trees(rec, seed=1):
+def start_trees(rec, seed=1, config="c2"):
+    """C1: path tree in clause order; C4: row-major path; C5: greedy tree; C2/C3: 4 spectral path trees."""
+    from tests import _instances
     from treesa_gpu_b200 import driver, engine, spectral
+    m = rec["m"]
+    if config in ("c1", "c4"):
+        return _instances.path_words(list(range(m)), m)[None, :]
+    if config == "c5":
+        return engine.tree_words(driver.dict_to_children(driver.greedy_tree(rec["ixs"], rec["iy"]), m))[None, :]
     so = spectral.spectral_orders(rec["ixs"], rec["iy"], k=4, seed=seed)
-    return np.stack([engine.tree_words(driver.dict_to_children(spectral.path_tree(o), rec["m"])) for _, _, o in so])
+    return np.stack([engine.tree_words(driver.dict_to_children(spectral.path_tree(o), m)) for _, _, o in so])
 
 
 def visits_per_step(W, world):
@@ -85,7 +126,7 @@ def cpu_reference_rate(W, trees, target_s=12.0):
     v, s = run(nlev)
     return dict(value=v / s, unit=UNIT, cores=threads, kind=kind,
                 sample=f"{nch} chains x first {nlev} of {len(betas)} levels x {W['niters']} sweeps "
-                       f"(sat100, spectral start, par), {s:.1f} s")
+                       f"({W['config']}, order {W['order']}), {s:.1f} s")
 
 
 # ------------------------------------------------------------------------------------------------
@@ -138,9 +179,9 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def ncu_traffic():
+def ncu_traffic(config="c2"):
     """DRAM bytes per launch of the sweep kernel from the committed ncu summary (None if absent)."""
-    p = os.path.join(ROOT, "profiles", "c2_sweep_ncu.json")
+    p = os.path.join(ROOT, "profiles", f"{config}_sweep_ncu.json")
     if os.path.exists(p):
         with open(p) as f:
             return json.load(f).get("dram_bytes_per_launch")
@@ -154,22 +195,24 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--chains", type=int, default=4096)
+    ap.add_argument("--chains", type=int, default=0, help="chains per GPU (default: the config's)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--levels", type=int, default=0, help="first L beta levels only (profiling runs)")
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS), help="BASELINE config (default c2)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    W = workload(args.chains)
+    nch = args.chains if args.chains > 0 else DEFAULT_CHAINS[args.config]
+    W = workload(nch, args.config)
     if args.levels > 0:
         W["betas"] = W["betas"][:args.levels]
 
     if args.impl == "reference":
         if rank != 0:
             return 0
-        trees = start_trees(W["rec"])
+        trees = start_trees(W["rec"], config=W["config"])
         for _ in range(args.warmup):
             cpu_reference_rate(W, trees, target_s=4.0)
         vals, t_total = [], 0.0
@@ -201,7 +244,7 @@ def main():
 
     rec = W["rec"]
     net = engine.Network(rec["ixs"], rec["iy"], rec["nlab"])
-    trees = start_trees(rec)
+    trees = start_trees(rec, config=W["config"])
     nccl_id = None
     if world > 1:
         obj = [engine.nccl_unique_id() if rank == 0 else None]
@@ -210,8 +253,10 @@ def main():
     stream = torch.cuda.current_stream()
     opts = dict(betas=W["betas"], niters=W["niters"], nchains=W["nchains"], sc_target=W["sc_target"],
                 order=W["order"], scheme=W["scheme"], seed=W["seed"], init_trees=trees, device=local,
+                slicing=W["slicing"],
                 stream=stream.cuda_stream, rank=rank, world_size=world, nccl_id=nccl_id)
     sess = engine.Session(net, **opts)
+    sess_info = sess.info()
     for _ in range(args.warmup):
         sess.reset()
         sess.run()
@@ -224,7 +269,8 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    kernel_s, launches, props, accs, visits_cnt = 0.0, 0, 0, 0, 0
+    kernel_s, launches = 0.0, 0
+    tot = dict(proposals=0, accepts=0, visits=0, chunks=0, chunks_acc=0, slice_proposals=0)
     for k in range(args.steps):
         flush.zero_()
         evs[k][0].record(stream)
@@ -234,9 +280,8 @@ def main():
         st = sess.stats()
         kernel_s += st["kernel_s"]
         launches += st["launches"]
-        props += st["proposals"]
-        accs += st["accepts"]
-        visits_cnt += st["visits"]
+        for key in tot:
+            tot[key] += st[key]
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -251,20 +296,34 @@ def main():
     vps = visits_per_step(W, world)
     value = args.steps * vps / T
 
-    # roofline of the dominant kernel (the sweep kernel): algorithmic bytes per visit (packed u64 bitsets)
+    # roofline of the dominant kernel (the sweep kernel).  Algorithmic bytes of the reference's algorithm
+    # on packed u64 bitsets: a visit without a rule reads its children word (4 B); a proposal reads the
+    # children of v and P (8 B) and five label sets (and S when slicing), and an accepted move writes
+    # P's set and two children words; with chunk summaries a set costs 16 B per chunk the move touches
+    # plus its summary; one whole-chain energy pass per level reads 3 sets and a children word per node.
+    info = sess_info
     nw64 = (rec["nlab"] + 63) // 64
     bset = 8 * nw64
     nint = rec["m"] - 1
-    lev_launches = launches  # one sweep launch per level per step (this rank)
-    alg = ((visits_cnt - props) * 4 + props * (8 + 5 * bset) + accs * (bset + 8)
-           + lev_launches * W["nchains"] * (nint * (3 * bset + 4) + bset))
+    P, A, V = tot["proposals"], tot["accepts"], tot["visits"]
+    if info["kernel"] == 2 and tot["chunks"] > 0:
+        sum_b = 8 if nw64 >= 32 else 0
+        sets = tot["chunks"] * 16 * (6 if W["slicing"] else 5) + P * 4 * sum_b
+        alg = (V - P) * 4 + P * 8 + sets + tot["chunks_acc"] * 16 + A * (8 + sum_b)
+    else:
+        alg = (V - P) * 4 + P * (8 + (6 if W["slicing"] else 5) * bset) + A * (bset + 8)
+    alg += launches * world * W["nchains"] * (nint * (3 * bset + 4) + bset)
+    alg_rank = alg / world  # the counters are summed over ranks, the kernel time is the slowest rank's
     peak, peak_kind = measured_peak()
-    achieved = alg / KS / 1e9  # GB/s over this rank's kernel time
-    trf = ncu_traffic()
+    achieved = alg_rank / KS / 1e9
+    trf = ncu_traffic(W["config"])
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": trf, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-            else "fallback", "kernel_visits_per_s": world * W["nchains"] * len(W["betas"]) * W["niters"] * nint *
-            args.steps / KS, "kernel_s": KS, "launches_per_step": launches // args.steps}
+            "traffic": trf, "peak_kind": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                                          else "fallback"),
+            "kernel": "k_anneal_warp" if info["kernel"] == 1 else "k_anneal_block",
+            "algorithmic_bytes_per_launch": alg_rank / max(1, launches),
+            "kernel_visits_per_s": world * W["nchains"] * len(W["betas"]) * W["niters"] * nint * args.steps / KS,
+            "kernel_s": KS, "launches_per_step": launches // args.steps}
 
     # e2e through the C ABI with host buffers
     e2e_t, h2d, d2h = 0.0, 0, 0

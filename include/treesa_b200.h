@@ -139,10 +139,12 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
 int tsa_session_reset(tsa_session* s, char* err, size_t errlen);
 void tsa_session_destroy(tsa_session* s);
 
-/* Per-run counters of the last tsa_session_run: [0] proposals, [1] accepts, [2] phases (warp steps),
- * [3] node visits, [4] slice proposals, [5] slice accepts, [6] busy lanes, [7] kernel launches,
- * [8] 16-byte label chunks the moves touched; and the summed device time of the sweep kernels. */
-int tsa_session_stats(tsa_session* s, uint64_t* counters9, double* kernel_seconds);
+/* Per-run counters of the last tsa_session_run (all ranks): [0] proposals, [1] accepts, [2] phases / work-
+ * list steps, [3] node visits, [4] slice proposals, [5] slice accepts, [6] busy lanes, [7] sweep-kernel
+ * launches (this rank), [8] 16-byte label chunks read by the proposals of the HBM kernel, [9] chunks
+ * written by its accepted moves, [10] host-to-device bytes, [11] device-to-host bytes (this rank); and
+ * the summed device time of the sweep kernels (this rank). */
+int tsa_session_stats(tsa_session* s, uint64_t* counters12, double* kernel_seconds);
 
 /* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
  * kernel (1 warp-per-chain, 2 CTA-per-chain), warps per CTA, grid, dynamic shared memory bytes}. */

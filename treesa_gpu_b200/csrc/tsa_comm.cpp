@@ -217,6 +217,10 @@ int Comm::fetch_record(const uint8_t* d_rec_local, uint32_t bytes, int owner, ui
 
 int Comm::sum_u64(uint64_t* host_vals, int n, cudaStream_t st, char* err, size_t errlen) {
   size_t cap = p->u64buf ? 16 : 0;
+  if (n > 16) {
+    cerr_set(err, errlen, "sum_u64: at most 16 values");
+    return TSA_ERR_ARG;
+  }
   int rc = grow(&p->u64buf, &cap, 16, err, errlen);
   if (rc) return rc;
   CCK(cudaMemcpyAsync(p->u64buf, host_vals, n * 8, cudaMemcpyHostToDevice, st));

@@ -454,7 +454,7 @@ struct tsa_session {
   std::vector<double> trace;
   std::vector<float> lc;
   std::vector<int> sc, ns;
-  uint64_t stats[9] = {0};
+  uint64_t stats[12] = {0};
   uint64_t launches = 0;
   uint64_t h2d = 0, d2h = 0;  // bytes copied between host and device by this session
 
@@ -531,7 +531,7 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
   for (auto& e : s->eve) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   CKR(cudaMalloc(&s->d_anc, s->nchains * sizeof(int)));
   CKR(cudaMalloc(&s->d_err, sizeof(int)));
-  CKR(cudaMalloc(&s->d_stats, 9 * sizeof(unsigned long long)));
+  CKR(cudaMalloc(&s->d_stats, 10 * sizeof(unsigned long long)));
   CKR(cudaEventCreate(&s->ev0));
   CKR(cudaEventCreate(&s->ev1));
   CKR(cudaMemcpyAsync(s->d_leaf, s->I.leaf.data(), s->I.leaf.size() * 8, cudaMemcpyHostToDevice, s->st));
@@ -611,7 +611,7 @@ int reset_run_state(tsa_session* s, char* err, size_t errlen) {
   s->trace.clear();
   s->launches = 0;
   memset(s->stats, 0, sizeof s->stats);
-  CKR(cudaMemsetAsync(s->d_stats, 0, 9 * sizeof(unsigned long long), s->st));
+  CKR(cudaMemsetAsync(s->d_stats, 0, 10 * sizeof(unsigned long long), s->st));
   CKR(cudaMemsetAsync(s->d_err, 0, sizeof(int), s->st));
   return TSA_OK;
 }
@@ -1017,15 +1017,18 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     memcpy(s->sc.data(), s->h_sc + off, nch * sizeof(int));
     memcpy(s->ns.data(), s->h_ns + off, nch * sizeof(int));
   }
-  unsigned long long st[9];
+  unsigned long long st[10];
   CKR(cudaMemcpy(st, s->d_stats, sizeof st, cudaMemcpyDeviceToHost));
   s->d2h += sizeof st;
-  for (int q = 0; q < 9; q++) s->stats[q] = st[q];
+  for (int q = 0; q < 10; q++) s->stats[q] = st[q];
   s->stats[7] = s->launches;
   if (s->world > 1) {
-    rc = s->comm->sum_u64(s->stats, 7, s->st, err, errlen);
+    rc = s->comm->sum_u64(s->stats, 10, s->st, err, errlen);
     if (rc) return rc;
+    s->stats[7] = s->launches;
   }
+  s->stats[10] = s->h2d;
+  s->stats[11] = s->d2h;
   s->t_anneal = now_s() - t0;
   s->ran = true;
   return TSA_OK;
@@ -1126,10 +1129,10 @@ int tsa_run(const tsa_instance* inst, const tsa_options* opt, tsa_result* res, c
   return rc;
 }
 
-int tsa_session_stats(tsa_session* s, uint64_t* c9, double* ksec) {
+int tsa_session_stats(tsa_session* s, uint64_t* c12, double* ksec) {
   if (!s) return TSA_ERR_ARG;
-  if (c9)
-    for (int q = 0; q < 9; q++) c9[q] = s->stats[q];
+  if (c12)
+    for (int q = 0; q < 12; q++) c12[q] = s->stats[q];
   if (ksec) *ksec = s->kernel_ms / 1e3;
   return TSA_OK;
 }

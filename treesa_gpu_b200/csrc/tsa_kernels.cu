@@ -138,7 +138,7 @@ struct WarpCtx {
 };
 
 struct Counters {
-  unsigned long long prop, acc, steps, visits, sprop, sacc, busy;
+  unsigned long long prop, acc, steps, visits, sprop, sacc, busy, chunks, chunks_acc;
 };
 
 // Metropolis: host-libm-exact (default) or with the device's expf as the reference's GPU binary
@@ -725,7 +725,12 @@ __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v
   int cP1 = sx + k2, cV1 = sd + k3;
   float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, B.sc_target, B.sc_weight, B.lse);
   bool acc = accept_rt(B.exp_device, B.beta, B.exptab, rnd.y, dE);
-  if (t == 0) cnt.prop++;
+  const int nck = SUMS ? __popcll(u) : B.nchunks;
+  if (t == 0) {
+    cnt.prop++;
+    cnt.chunks += nck;
+    if (acc) cnt.chunks_acc += nck;
+  }
   if (!acc) return;
   uint64_t xs = 0;
   for_chunks<SUMS>(u, B.nchunks, G, t, [&](int c) {
@@ -1123,18 +1128,20 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
     __syncthreads();
   }
   // every thread: its own proposals/accepts/visits; steps and slice moves counted by one thread/warp
-  unsigned long long v[7] = {cnt.prop, cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc, cnt.busy};
+  unsigned long long v[9] = {cnt.prop,  cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc,
+                             cnt.busy, cnt.chunks, cnt.chunks_acc};
 #pragma unroll
-  for (int q = 0; q < 7; q++) {
+  for (int q = 0; q < 9; q++) {
     for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(FULL, v[q], o);
   }
   if (lane == 0) {
     // slice moves were counted by all 32 lanes of warp 0
     v[4] /= 32;
     v[5] /= 32;
+    const int slot[9] = {0, 1, 2, 3, 4, 5, 6, 8, 9};
 #pragma unroll
-    for (int q = 0; q < 7; q++)
-      if (v[q]) atomicAdd(&a.stats[q], v[q]);
+    for (int q = 0; q < 9; q++)
+      if (v[q]) atomicAdd(&a.stats[slot[q]], v[q]);
   }
 }
 

@@ -42,7 +42,7 @@ struct SweepArgs {
   float* out_lc;             // [nchains] per-chain energy after the launch
   int* out_sc;
   int* out_ns;
-  unsigned long long* stats; // 9 counters (see tsa_session_stats)
+  unsigned long long* stats; // 10 device counters (see tsa_session_stats; [7] is host-side)
   int* err;                  // nonzero: a bounded wait timed out
   const float* lse_tab;      // 64 floats (device)
   const uint64_t* leaf_sum;  // [m] chunk summaries of the leaf sets (when L.sums)

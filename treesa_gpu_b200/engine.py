@@ -87,11 +87,11 @@ class Session:
         return rc, d
 
     def stats(self):
-        c = (C.c_uint64 * 9)()
+        c = (C.c_uint64 * 12)()
         ks = C.c_double()
         self.L.tsa_session_stats(self.h, c, C.byref(ks))
         names = ["proposals", "accepts", "phases", "visits", "slice_proposals", "slice_accepts", "busy_lanes",
-                 "launches", "chunks"]
+                 "launches", "chunks", "chunks_acc", "h2d_bytes", "d2h_bytes"]
         d = {k: int(v) for k, v in zip(names, c)}
         d["kernel_s"] = ks.value
         return d
