@@ -85,8 +85,9 @@ typedef struct tsa_options {
   int32_t exp_mode;           /* Metropolis expf: 0 = the host libm's (bit-exact with the reference's CPU port
                                  csrc/cpu_ref.h, default); 1 = the device's expf (bit-exact with the
                                  reference's GPU binary, csrc/common.h:228 compiled by nvcc) */
-  int32_t kernel_hint;        /* 0 auto; 1 warp-per-chain kernel (chain in shared memory); 2 CTA-per-chain
-                                 kernel (label sets in HBM).  Never changes a result. */
+  int32_t kernel_hint;        /* 0 auto; 1 one warp per chain (chain in shared memory); 2 one CTA per chain
+                                 (label sets in HBM); 3 two warps per chain (par order).  Never changes a
+                                 result. */
   int32_t reserved[12];
 } tsa_options;
 

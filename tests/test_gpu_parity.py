@@ -44,12 +44,14 @@ def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None, kerne
 WIDE = ["grid24", "grid28", "sq46"]  # 576, 784 and 4140 labels: CTA-per-chain kernel (sq46 with summaries)
 
 
-@pytest.mark.parametrize("kernel", ["warp", "block"])
+@pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
 @pytest.mark.parametrize("order", ["par", "preorder"])
 @pytest.mark.parametrize("name", SMALL + WIDE)
 def test_trajectories_bit_exact(name, order, kernel):
-    if name in WIDE and kernel == "warp":
-        pytest.skip("wide label sets have no warp-kernel layout")
+    if name in WIDE and kernel != "block":
+        pytest.skip("wide label sets have no shared-memory layout")
+    if kernel == "pair" and order == "preorder":
+        pytest.skip("two warps per chain is the par-order kernel")
     rec = _util.instance(name)
     net, onet = _net(rec)
     nch = 16 if name in WIDE else 64
@@ -132,12 +134,12 @@ def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
         assert abs(od["tc"] - d["tc"]) < 1e-9 and od["sc"] == d["sc"]
 
 
-@pytest.mark.parametrize("kernel", ["warp", "block"])
+@pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
 @pytest.mark.parametrize("name", ["sat100", "reg3_250", "grid24"])
 def test_fixed_slice_set_bit_exact(name, kernel):
     """A fixed slice set (labels of size 1): every cost on the sliced network (reference check section C)."""
     rec = _util.instance(name)
-    if name == "grid24" and kernel == "warp":
+    if name == "grid24" and kernel != "block":
         pytest.skip("wide")
     net, onet = _net(rec)
     rng = np.random.default_rng(8)
@@ -153,13 +155,13 @@ def test_fixed_slice_set_bit_exact(name, kernel):
     assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
 
 
-@pytest.mark.parametrize("kernel", ["warp", "block"])
+@pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
 @pytest.mark.parametrize("name,T", [("sat60", 30), ("reg3_250", 24), ("grid24", 34)])
 def test_slice_moves_match_oracle(name, T, kernel):
     """Annealed slice sets (reference test (4) configurations).  The slice-move Metropolis test reads float
     energies (device log2f/exp2f on the GPU, libm on the host); they differ in the last bit at most, which
     changes a decision with probability ~1e-7 per proposal, so these runs agree exactly."""
-    if name == "grid24" and kernel == "warp":
+    if name == "grid24" and kernel != "block":
         pytest.skip("wide")
     rec = _util.instance(name)
     net, onet = _net(rec)

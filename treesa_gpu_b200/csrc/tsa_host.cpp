@@ -510,7 +510,8 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
     CKR(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     s->own_stream = true;
   }
-  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, &s->plan) != cudaSuccess) {
+  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, s->order, s->slice_moves, &s->plan) !=
+      cudaSuccess) {
     set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
     return TSA_ERR_UNSUPPORTED;
   }
@@ -781,7 +782,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   std::iota(family.begin(), family.end(), 0);
   std::mt19937_64 hrng(splitmix64(s->seed + 777));
   float beta_last = s->betas[0];
-  const bool pipelined = s->scheme == TSA_SCHEME_INDEP && s->plan.kind == tsa::K_WARP;
+  const bool pipelined = s->scheme == TSA_SCHEME_INDEP && s->plan.kind != tsa::K_BLOCK;
   tsa::SweepArgs a{};
   a.L = s->L;
   a.leaf = s->d_leaf;
@@ -1100,7 +1101,8 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
   res->ntrace = (int)(s->trace.size() / 10);
   res->trace = (double*)malloc(sizeof(double) * std::max<size_t>(1, s->trace.size()));
   if (!s->trace.empty()) memcpy(res->trace, s->trace.data(), s->trace.size() * 8);
-  snprintf(res->kernel, sizeof res->kernel, "%s", s->plan.kind == tsa::K_WARP ? "warp_smem" : "block_hbm");
+  snprintf(res->kernel, sizeof res->kernel, "%s",
+           s->plan.kind == tsa::K_WARP ? "warp_smem" : s->plan.kind == tsa::K_PAIR ? "pair_smem" : "block_hbm");
   res->h2d_bytes = s->h2d;
   res->d2h_bytes = s->d2h;
   return valid && labels_ok ? TSA_OK : TSA_ERR_INVALID;
@@ -1143,7 +1145,7 @@ int tsa_session_info(tsa_session* s, int32_t* v) {
   v[1] = s->L.nint;
   v[2] = s->L.nw;
   v[3] = (int32_t)s->L.rec_bytes;
-  v[4] = s->plan.kind == tsa::K_WARP ? 1 : 2;
+  v[4] = s->plan.kind == tsa::K_WARP ? 1 : s->plan.kind == tsa::K_BLOCK ? 2 : 3;
   v[5] = s->plan.warps_per_cta;
   v[6] = s->plan.grid;
   v[7] = (int32_t)s->plan.smem;

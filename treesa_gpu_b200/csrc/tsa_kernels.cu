@@ -602,6 +602,234 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
 }
 
 
+
+// ================================================================================================
+// k_anneal_pair<NW>: par order with two warps per chain (64 lanes), so that twice as many warps are
+// resident for the same shared memory; registers are capped for 14 pairs per SM.  Same chain slot as
+// k_anneal_warp plus a second unvisited list: the phase scan compacts with shared-memory atomics
+// (entries land in any order; the moves of one phase commute), and the two warps meet at a named
+// barrier after the scan and after the visits of every phase.
+// ================================================================================================
+struct PairSmem {
+  uint32_t off_bar, off_cnt, off_leaf, off_slots, slot_bytes, off_scr, total;
+  int nint2;
+  __host__ __device__ static PairSmem make(const Layout& L, int npairs, int slice_moves) {
+    PairSmem w;
+    w.nint2 = (int)rnd_up((uint32_t)L.nint, 8);
+    w.off_bar = 768;  // [0,256) lse, [256,768) exp
+    w.off_cnt = rnd_up(w.off_bar + 8u * (uint32_t)npairs, 16);
+    w.off_leaf = rnd_up(w.off_cnt + 32u * (uint32_t)npairs, 128);
+    w.off_slots = rnd_up(w.off_leaf + (uint32_t)L.m * (uint32_t)L.nw * 8u, 128);
+    // record, then pri / par / wl / U / U2 (u16), then the cz scratch of slice moves
+    w.off_scr = L.rec_bytes + 10u * (uint32_t)w.nint2;
+    w.slot_bytes = rnd_up(w.off_scr + (slice_moves > 0 ? 4u * (uint32_t)w.nint2 : 0u), 128);
+    w.total = w.off_slots + w.slot_bytes * (uint32_t)npairs;
+    return w;
+  }
+};
+
+template <int NW>
+__global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const Layout L = a.L;
+  const PairSmem W = PairSmem::make(L, npairs, a.slice_moves);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, pair = warp >> 1, sub = warp & 1;
+  const int pl = threadIdx.x & 63;
+  const uint32_t bid = 1u + (uint32_t)pair;
+  float* s_lse = reinterpret_cast<float*>(smem);
+  double* s_exp = reinterpret_cast<double*>(smem + 256);
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + W.off_bar);
+  int* pc = reinterpret_cast<int*>(smem + W.off_cnt) + 8 * pair;  // [0..2] even phases, [4..6] odd, [7] fail
+  uint64_t* s_leaf = reinterpret_cast<uint64_t*>(smem + W.off_leaf);
+  for (int t = threadIdx.x; t < 64; t += blockDim.x) {
+    s_lse[t] = a.lse_tab[t];
+    s_exp[t] = c_exp_tab[t];
+  }
+  for (int t = threadIdx.x; t < L.m * NW; t += blockDim.x) s_leaf[t] = a.leaf[t];
+  if (pl == 0) {
+    mbar_init(&s_bar[pair], 1);
+    for (int q = 0; q < 8; q++) pc[q] = 0;
+  }
+  fence_proxy_async();
+  __syncthreads();
+  auto psync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bid) : "memory"); };
+
+  WarpCtx X_;
+  X_.m = L.m;
+  X_.nint = L.nint;
+  X_.key0 = a.key0;
+  X_.key1 = a.key1;
+  X_.beta = a.beta;
+  X_.sc_target = a.sc_target;
+  X_.sc_weight = a.sc_weight;
+  X_.slicing = a.slicing;
+  X_.exp_device = a.exp_device;
+  X_.lse = s_lse;
+  X_.exptab = s_exp;
+  X_.leaf = s_leaf;
+
+  uint8_t* slot = smem + W.off_slots + (size_t)pair * W.slot_bytes;
+  uint64_t* lab = reinterpret_cast<uint64_t*>(slot);
+  uint32_t* ch = reinterpret_cast<uint32_t*>(slot + L.off_ch);
+  uint32_t* cz = reinterpret_cast<uint32_t*>(slot + L.off_cz);
+  uint64_t* S = reinterpret_cast<uint64_t*>(slot + L.off_S);
+  uint16_t* pri = reinterpret_cast<uint16_t*>(slot + L.rec_bytes);
+  uint16_t* par = pri + W.nint2;
+  uint16_t* wl = par + W.nint2;
+  uint16_t* Ua = wl + W.nint2;
+  uint16_t* Ub = Ua + W.nint2;
+  uint32_t* cz2 = reinterpret_cast<uint32_t*>(slot + W.off_scr);
+  const int m = L.m, nint = L.nint, nint2 = W.nint2;
+  const unsigned FULL = 0xFFFFFFFFu;
+  const unsigned lt = (1u << lane) - 1u;
+  Counters cnt{};
+  uint32_t phase = 0;
+
+  for (int c = blockIdx.x * npairs + pair; c < a.nchains; c += gridDim.x * npairs) {
+    uint8_t* grec = a.recs + (size_t)c * L.rec_bytes;
+    if (pl == 0) {
+      fence_proxy_async();
+      mbar_expect_tx(&s_bar[pair], L.rec_bytes);
+      bulk_g2s(slot, grec, L.rec_bytes, &s_bar[pair]);
+    }
+    bool ok = mbar_wait(&s_bar[pair], phase);
+    phase ^= 1u;
+    if (lane == 0 && !__all_sync(FULL, ok)) atomicOr(&pc[7], 1);
+    else if (lane != 0) (void)__all_sync(FULL, ok);
+    psync();
+    if (pc[7]) {
+      if (pl == 0) atomicExch(a.err, 1);
+      break;
+    }
+    const uint32_t chain = (uint32_t)(a.chain0 + c);
+    const uint32_t hc = chain_hash(chain, a.key0);
+    for (int i = pl; i < nint; i += 64) {
+      uint32_t cw = ch[i];
+      int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+      if (l >= m) par[l - m] = (uint16_t)(m + i);
+      if (r >= m) par[r - m] = (uint16_t)(m + i);
+    }
+    if (pl == 0) par[nint - 1] = 0xFFFFu;
+    psync();
+    for (int s = 0; s < a.nsweeps; s++) {
+      const uint32_t sw = a.sweep0 + (uint32_t)s;
+      const uint32_t hs = sweep_hash(sw, hc);
+      for (int i = pl; i < nint; i += 64) {
+        pri[i] = (uint16_t)node_pri((uint32_t)(m + i), hs);
+        Ua[i] = (uint16_t)i;
+      }
+      uint16_t *U = Ua, *U2 = Ub;
+      int nU = nint;
+      psync();
+      for (int ph = 0; ph <= nint; ph++) {
+        int* cur = pc + 4 * (ph & 1);
+        int* nxt = pc + 4 * ((ph + 1) & 1);
+        for (int base = 0; base < nU; base += 64) {
+          int j = base + pl;
+          bool valid = j < nU;
+          int i = valid ? (int)U[j] : 0;
+          bool act = false;
+          uint32_t cw = 0;
+          if (valid) {
+            uint32_t key = ((uint32_t)pri[i] << 16) | (uint32_t)(m + i);
+            act = true;
+            int p = par[i];
+            if (p != 0xFFFF) {
+              uint32_t pp = pri[p - m];
+              if (pp && ((pp << 16) | (uint32_t)p) > key) act = false;
+            }
+            cw = ch[i];
+            int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+            if (act && l >= m) {
+              uint32_t pq = pri[l - m];
+              if (pq && ((pq << 16) | (uint32_t)l) > key) act = false;
+            }
+            if (act && r >= m) {
+              uint32_t pq = pri[r - m];
+              if (pq && ((pq << 16) | (uint32_t)r) > key) act = false;
+            }
+          }
+          bool cher = act && (int)(cw & 0xFFFFu) < m && (int)(cw >> 16) < m;
+          bool prop = act && !cher;
+          bool keep = valid && !act;
+          unsigned ba = __ballot_sync(FULL, prop), bc = __ballot_sync(FULL, cher), bk = __ballot_sync(FULL, keep);
+          int p0 = 0, p1 = 0, p2 = 0;
+          if (lane == 0) {
+            if (ba) p0 = atomicAdd(&cur[0], __popc(ba));
+            if (bc) p1 = atomicAdd(&cur[1], __popc(bc));
+            if (bk) p2 = atomicAdd(&cur[2], __popc(bk));
+          }
+          p0 = __shfl_sync(FULL, p0, 0);
+          p1 = __shfl_sync(FULL, p1, 0);
+          p2 = __shfl_sync(FULL, p2, 0);
+          if (prop) wl[p0 + __popc(ba & lt)] = (uint16_t)i;
+          if (cher) wl[nint2 - 1 - (p1 + __popc(bc & lt))] = (uint16_t)i;
+          if (keep) U2[p2 + __popc(bk & lt)] = (uint16_t)i;
+        }
+        if (pl == 0) {
+          nxt[0] = 0;
+          nxt[1] = 0;
+          nxt[2] = 0;
+        }
+        psync();
+        const int nk = cur[0], nc = cur[1];
+        nU = cur[2];
+        uint16_t* tmp = U;
+        U = U2;
+        U2 = tmp;
+        if (nk + nc == 0) break;
+        if (pl == 0) {
+          cnt.steps++;
+          cnt.busy += nk;
+        }
+        for (int j = pl; j < nc; j += 64) {
+          pri[wl[nint2 - 1 - j]] = 0;
+          cnt.visits++;
+        }
+        for (int j = pl; j < nk; j += 64) {
+          int i = wl[j];
+          visit<NW, true>(X_, lab, ch, cz, S, par, m + i, sw, chain, cnt);
+          pri[i] = 0;
+          cnt.visits++;
+        }
+        psync();
+      }
+      if (a.slice_moves > 0 && (sw + 1) % (uint32_t)a.slice_every == 0) {
+        if (sub == 0) slice_step<NW>(X_, a, lab, ch, cz, cz2, S, sw, chain, lane, cnt);
+        psync();
+      }
+    }
+    if (sub == 0) {
+      EvalOut e = eval_cached<NW>(X_, cz, S, a.leaf_sc, lane);
+      if (lane == 0) {
+        a.out_lc[c] = e.lcost;
+        a.out_sc[c] = e.sc;
+        a.out_ns[c] = e.ns;
+      }
+    }
+    psync();
+    if (pl == 0) {
+      fence_proxy_async();
+      bulk_s2g(a.recs_out + (size_t)c * L.rec_bytes, slot, L.rec_bytes);
+      bulk_wait_read();
+    }
+    psync();
+  }
+  if (pl == 0) bulk_wait_all();
+  // proposals, accepts, visits per lane; phases, busy lanes once per pair; slice moves by all of warp 0
+  unsigned long long v[7] = {cnt.prop, cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc, cnt.busy};
+  for (int o = 16; o > 0; o >>= 1) {
+    v[0] += __shfl_xor_sync(FULL, v[0], o);
+    v[1] += __shfl_xor_sync(FULL, v[1], o);
+    v[3] += __shfl_xor_sync(FULL, v[3], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < 7; q++)
+      if (v[q]) atomicAdd(&a.stats[q], v[q]);
+  }
+}
+
 // ================================================================================================
 // k_anneal_block: one CTA per chain for chains that do not fit in shared memory.  Per-node metadata
 // (children, (cost, size), chunk summaries, priorities, parents, work lists) in shared memory; label
@@ -1164,6 +1392,27 @@ static cudaError_t launch_warp_t(const SweepArgs& a, const LaunchPlan& p, cudaSt
   return cudaGetLastError();
 }
 
+template <int NW>
+static cudaError_t launch_pair_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
+  auto k = k_anneal_pair<NW>;
+  size_t smem = PairSmem::make(a.L, p.warps_per_cta, a.slice_moves).total;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<p.grid, 64 * p.warps_per_cta, smem, st>>>(a, p.warps_per_cta);
+  return cudaGetLastError();
+}
+
+static cudaError_t launch_pair(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
+  switch (a.L.nw) {
+    case 1: return launch_pair_t<1>(a, p, st);
+    case 2: return launch_pair_t<2>(a, p, st);
+    case 4: return launch_pair_t<4>(a, p, st);
+    case 6: return launch_pair_t<6>(a, p, st);
+    case 8: return launch_pair_t<8>(a, p, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <int ORDER>
 static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
   switch (a.L.nw) {
@@ -1186,13 +1435,32 @@ static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaS
   return cudaGetLastError();
 }
 
-cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, LaunchPlan* plan) {
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
+                        LaunchPlan* plan) {
   int nsm = 0, optin = 0;
   cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   if (e != cudaSuccess) return e;
   bool warp_ok = (L.nw == 1 || L.nw == 2 || L.nw == 4 || L.nw == 6 || L.nw == 8) && hint != 2;
+  // par order: two warps per chain (up to 14 pairs per SM)
+  if (warp_ok && order == 0 && (hint == 0 || hint == 3)) {
+    int np = 14;
+    while (np > 0 && PairSmem::make(L, np, slice_moves).total > (uint32_t)optin) np--;
+    if (np > 0) {
+      int need = (nchains + np - 1) / np;
+      while (np > 1 && need < nsm) {
+        np = (np + 1) / 2;
+        need = (nchains + np - 1) / np;
+      }
+      plan->kind = K_PAIR;
+      plan->warps_per_cta = np;
+      plan->grid = need < nsm ? need : nsm;
+      plan->smem = PairSmem::make(L, np, slice_moves).total;
+      return cudaSuccess;
+    }
+  }
+  if (hint == 3) return cudaErrorNotSupported;
   if (warp_ok) {
     // as many chain slots per CTA as fit (at most 16 warps), one CTA per SM
     int wpc = 16;
@@ -1223,6 +1491,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, Laun
 }
 
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
+  if (p.kind == K_PAIR) return launch_pair(a, p, st);
   if (p.kind == K_WARP) return a.order == 0 ? launch_warp_o<0>(a, p, st) : launch_warp_o<1>(a, p, st);
   if (a.L.sums) return a.order == 0 ? launch_block_t<true, 0>(a, p, st) : launch_block_t<true, 1>(a, p, st);
   return a.order == 0 ? launch_block_t<false, 0>(a, p, st) : launch_block_t<false, 1>(a, p, st);

@@ -49,17 +49,19 @@ struct SweepArgs {
 };
 
 // Kernel family chosen by the host for a layout.
-enum KernelKind { K_WARP = 0, K_BLOCK = 1 };
+enum KernelKind { K_WARP = 0, K_BLOCK = 1, K_PAIR = 2 };
 
 struct LaunchPlan {
   KernelKind kind;
-  int warps_per_cta;         // chains per CTA (K_WARP) or warps per chain (K_BLOCK)
+  int warps_per_cta;         // chains per CTA (K_WARP), warps per chain (K_BLOCK), chain pairs (K_PAIR)
   int grid;
   size_t smem;
 };
 
 // Host-side entry points (tsa_kernels.cu).
-cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, LaunchPlan* plan);
+// hint: 0 auto, 1 one warp per chain, 2 one CTA per chain (label sets in HBM), 3 two warps per chain
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
+                        LaunchPlan* plan);
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
                                cudaStream_t st);
