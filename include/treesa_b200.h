@@ -147,6 +147,16 @@ void tsa_session_destroy(tsa_session* s);
  * the summed device time of the sweep kernels (this rank). */
 int tsa_session_stats(tsa_session* s, uint64_t* counters12, double* kernel_seconds);
 
+/* Population resampling of caller-held chain records (the reference's Runner::resample,
+ * csrc/treesa_gpu.cu:1925-1933, and its k_copy, :1017-1022): every record c becomes a copy of record
+ * anc[c], all at once.  records: device pointer to nchains records of rec_bytes bytes each (rec_bytes a
+ * multiple of 16, e.g. info8[3] of a session); anc: host array of nchains ancestors in [0, nchains);
+ * stream: cudaStream_t or NULL (the legacy stream) of the device that holds the records.  The gather goes
+ * through a scratch copy of the population that the call allocates and frees; it returns when the
+ * records hold their ancestors. */
+int tsa_resample(void* records, const int32_t* anc, int32_t nchains, uint32_t rec_bytes, void* stream, char* err,
+                 size_t errlen);
+
 /* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
  * kernel (1 warp-per-chain, 2 CTA-per-chain), warps per CTA, grid, dynamic shared memory bytes}. */
 int tsa_session_info(tsa_session* s, int32_t* info8);

@@ -8,6 +8,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -122,20 +123,29 @@ static int grow(T** buf, size_t* cap, size_t need, char* err, size_t errlen) {
   return TSA_OK;
 }
 
-Comm::~Comm() {
-  if (!p) return;
-  cudaSetDevice(p->device);
-  if (p->comm) p->N->commDestroy(p->comm);
-  cudaFree(p->g_lc);
-  cudaFree(p->g_sc);
-  cudaFree(p->g_ns);
-  cudaFree(p->sendbuf);
-  cudaFree(p->recvbuf);
-  cudaFree(p->recbuf);
-  cudaFree(p->u64buf);
-  cudaFree(p->d_idx);
-  delete p;
+// Communicators are kept for the life of the process, keyed by (unique id, rank, world, device): a caller
+// that passes the same id again (every rank does) reuses the communicator instead of re-initializing
+// NCCL.  Two sessions must not use the same communicator at the same time.
+namespace {
+struct CommKey {
+  char id[128];
+  int rank, world, device;
+  bool operator<(const CommKey& o) const {
+    int c = memcmp(id, o.id, sizeof id);
+    if (c) return c < 0;
+    if (rank != o.rank) return rank < o.rank;
+    if (world != o.world) return world < o.world;
+    return device < o.device;
+  }
+};
+std::mutex g_comm_mu;
+std::map<CommKey, CommImpl*>& comm_cache() {
+  static std::map<CommKey, CommImpl*> m;
+  return m;
 }
+}  // namespace
+
+Comm::~Comm() {}  // the cached CommImpl outlives the session
 
 int comm_unique_id(void* id128, char* err, size_t errlen) {
   const Nccl* N = nccl(err, errlen);
@@ -158,26 +168,40 @@ int comm_create(const void* id128, int rank, int world, int device, Comm** out, 
   }
   const Nccl* N = nccl(err, errlen);
   if (!N) return TSA_ERR_COMM;
-  Comm* c = new Comm();
-  c->p = new CommImpl();
-  c->rank = rank;
-  c->world = world;
-  CommImpl* p = c->p;
-  p->N = N;
-  p->device = device;
   if (cudaSetDevice(device) != cudaSuccess) {
     cerr_set(err, errlen, "cudaSetDevice(%d) failed", device);
-    delete c;
     return TSA_ERR_CUDA;
   }
-  ncclUniqueId id;
-  memcpy(&id, id128, sizeof id);
-  ncclResult_t r = N->commInitRank(&p->comm, world, id, rank);
-  if (r != ncclSuccess) {
-    cerr_set(err, errlen, "ncclCommInitRank: %s", N->errStr(r));
-    delete c;
-    return TSA_ERR_COMM;
+  CommKey key;
+  memcpy(key.id, id128, sizeof key.id);
+  key.rank = rank;
+  key.world = world;
+  key.device = device;
+  CommImpl* p = nullptr;
+  {
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    auto it = comm_cache().find(key);
+    if (it != comm_cache().end()) p = it->second;
   }
+  if (!p) {
+    p = new CommImpl();
+    p->N = N;
+    p->device = device;
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof id);
+    ncclResult_t r = N->commInitRank(&p->comm, world, id, rank);
+    if (r != ncclSuccess) {
+      cerr_set(err, errlen, "ncclCommInitRank: %s", N->errStr(r));
+      delete p;
+      return TSA_ERR_COMM;
+    }
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    comm_cache()[key] = p;
+  }
+  Comm* c = new Comm();
+  c->p = p;
+  c->rank = rank;
+  c->world = world;
   *out = c;
   return TSA_OK;
 }

@@ -1139,6 +1139,37 @@ int tsa_session_stats(tsa_session* s, uint64_t* c12, double* ksec) {
   return TSA_OK;
 }
 
+int tsa_resample(void* records, const int32_t* anc, int32_t nchains, uint32_t rec_bytes, void* stream, char* err,
+                 size_t errlen) {
+  if (!records || !anc || nchains < 1 || rec_bytes == 0 || rec_bytes % 16) {
+    set_err(err, errlen, "tsa_resample: need records, anc, nchains >= 1 and rec_bytes a positive multiple of 16");
+    return TSA_ERR_ARG;
+  }
+  for (int c = 0; c < nchains; c++)
+    if (anc[c] < 0 || anc[c] >= nchains) {
+      set_err(err, errlen, "tsa_resample: ancestor %d of chain %d out of range", anc[c], c);
+      return TSA_ERR_ARG;
+    }
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t bytes = (size_t)nchains * rec_bytes;
+  uint8_t* scratch = nullptr;
+  int* d_anc = nullptr;
+  cudaError_t e = cudaMalloc(&scratch, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&d_anc, nchains * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_anc, anc, nchains * sizeof(int), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess)
+    e = tsa::launch_copy_chains(static_cast<const uint8_t*>(records), scratch, d_anc, nchains, rec_bytes, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(records, scratch, bytes, cudaMemcpyDeviceToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  cudaFree(scratch);
+  cudaFree(d_anc);
+  if (e != cudaSuccess) {
+    set_err(err, errlen, "tsa_resample: CUDA error %s", cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? TSA_ERR_NOMEM : TSA_ERR_CUDA;
+  }
+  return TSA_OK;
+}
+
 int tsa_session_info(tsa_session* s, int32_t* v) {
   if (!s || !v) return TSA_ERR_ARG;
   v[0] = s->L.m;

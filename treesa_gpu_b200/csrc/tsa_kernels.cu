@@ -75,17 +75,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 __host__ __device__ inline uint32_t rnd_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
 struct WarpSmem {
-  uint32_t off_bar, off_leaf, off_slots, slot_bytes, off_scr, total;
-  int nint2;
-  __host__ __device__ static WarpSmem make(const Layout& L, int wpc) {
+  uint32_t off_bar, off_leaf, off_slots, slot_bytes, off_par, off_scr, total;
+  int nint2, nkey;
+  __host__ __device__ static WarpSmem make(const Layout& L, int wpc, int slice_moves) {
     WarpSmem w;
     w.nint2 = (int)rnd_up((uint32_t)L.nint, 8);
+    w.nkey = (int)rnd_up((uint32_t)L.nint + 1u, 4);  // par-order keys + a zero sentinel at [nint]
     w.off_bar = 768;  // [0,256): lse table, [256,768): exp table
     w.off_leaf = rnd_up(w.off_bar + 8u * (uint32_t)wpc, 128);
     w.off_slots = rnd_up(w.off_leaf + (uint32_t)L.m * (uint32_t)L.nw * 8u, 128);
-    // record, then pri / par / wl / U (u16 each), then a cz scratch for slice moves
-    w.off_scr = L.rec_bytes + 8u * (uint32_t)w.nint2;
-    w.slot_bytes = rnd_up(w.off_scr + 4u * (uint32_t)w.nint2, 128);
+    // record, then key (u32), par / wl / U (u16 each), then a cz scratch for slice moves
+    w.off_par = L.rec_bytes + 4u * (uint32_t)w.nkey;
+    w.off_scr = w.off_par + 6u * (uint32_t)w.nint2;
+    w.slot_bytes = rnd_up(w.off_scr + (slice_moves > 0 ? 4u * (uint32_t)w.nint2 : 0u), 128);
     w.total = w.off_slots + w.slot_bytes * (uint32_t)wpc;
     return w;
   }
@@ -382,7 +384,7 @@ template <int NW, int ORDER>
 __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L = a.L;
-  const WarpSmem W = WarpSmem::make(L, wpc);
+  const WarpSmem W = WarpSmem::make(L, wpc, a.slice_moves);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* s_lse = reinterpret_cast<float*>(smem);
   double* s_exp = reinterpret_cast<double*>(smem + 256);
@@ -419,8 +421,8 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   uint32_t* ch = reinterpret_cast<uint32_t*>(slot + L.off_ch);
   uint32_t* cz = reinterpret_cast<uint32_t*>(slot + L.off_cz);
   uint64_t* S = reinterpret_cast<uint64_t*>(slot + L.off_S);
-  uint16_t* pri = reinterpret_cast<uint16_t*>(slot + L.rec_bytes);
-  uint16_t* par = pri + W.nint2;
+  uint32_t* key = reinterpret_cast<uint32_t*>(slot + L.rec_bytes);
+  uint16_t* par = reinterpret_cast<uint16_t*>(slot + W.off_par);
   uint16_t* wl = par + W.nint2;
   uint16_t* U = wl + W.nint2;
   uint32_t* cz2 = reinterpret_cast<uint32_t*>(slot + W.off_scr);
@@ -462,64 +464,62 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
       if (ORDER == 0) {
         // ---- par order: phases of independent sets (cpu_ref.h:133-182, k_par :897-972) ----
+        // key[i] = priority << 16 | node id while node m+i is unvisited, 0 once visited; key[nint] = 0 is
+        // the sentinel read for a leaf child or the root's parent, so a node is active iff its key
+        // exceeds the keys of its parent and children.
         const uint32_t hs = sweep_hash(sw, hc);
         for (int i = lane; i < nint; i += 32) {
-          pri[i] = (uint16_t)node_pri((uint32_t)(m + i), hs);
+          key[i] = (node_pri((uint32_t)(m + i), hs) << 16) | (uint32_t)(m + i);
           U[i] = (uint16_t)i;
         }
+        if (lane == 0) key[nint] = 0u;
         int nU = nint;
         __syncwarp();
         for (int guard = 0; guard <= nint; guard++) {
           int nk = 0, nu = 0, nc = 0;
-          for (int base = 0; base < nU; base += 32) {
-            int j = base + lane;
-            bool valid = j < nU;
-            int i = valid ? (int)U[j] : 0;
-            bool act = false;
-            if (valid) {
-              uint32_t key = ((uint32_t)pri[i] << 16) | (uint32_t)(m + i);
-              act = true;
-              int p = par[i];
-              if (p != 0xFFFF) {
-                uint32_t pp = pri[p - m];
-                if (pp && ((pp << 16) | (uint32_t)p) > key) act = false;
-              }
-              uint32_t cw = ch[i];
-              int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
-              if (act && l >= m) {
-                uint32_t pl = pri[l - m];
-                if (pl && ((pl << 16) | (uint32_t)l) > key) act = false;
-              }
-              if (act && r >= m) {
-                uint32_t pr = pri[r - m];
-                if (pr && ((pr << 16) | (uint32_t)r) > key) act = false;
-              }
-            }
-            // active nodes whose children are both leaves make no proposal: they only become visited
-            bool cher = act && (int)(ch[i] & 0xFFFFu) < m && (int)(ch[i] >> 16) < m;
-            bool prop = act && !cher;
-            unsigned ba = __ballot_sync(FULL, prop), bc = __ballot_sync(FULL, cher),
-                     bk = __ballot_sync(FULL, valid && !act);
+          // two list entries per lane per step: their shared-memory loads overlap
+          for (int base = 0; base < nU; base += 64) {
+            const int j0 = base + lane, j1 = base + 32 + lane;
+            const bool v0 = j0 < nU, v1 = j1 < nU;
+            const int i0 = v0 ? (int)U[j0] : nint, i1 = v1 ? (int)U[j1] : nint;
+            const uint32_t k0 = key[i0], k1 = key[i1];
+            const uint32_t c0 = ch[v0 ? i0 : 0], c1 = ch[v1 ? i1 : 0];
+            const int p0 = par[v0 ? i0 : 0], p1 = par[v1 ? i1 : 0];
+            auto idx = [&](int n) { return n >= m ? n - m : nint; };
+            const int l0 = (int)(c0 & 0xFFFFu), r0 = (int)(c0 >> 16), l1 = (int)(c1 & 0xFFFFu), r1 = (int)(c1 >> 16);
+            const uint32_t q0 = max(key[p0 == 0xFFFF ? nint : p0 - m], max(key[idx(l0)], key[idx(r0)]));
+            const uint32_t q1 = max(key[p1 == 0xFFFF ? nint : p1 - m], max(key[idx(l1)], key[idx(r1)]));
+            const bool a0 = v0 && k0 > q0, a1 = v1 && k1 > q1;
+            const bool ch0 = a0 && l0 < m && r0 < m, ch1 = a1 && l1 < m && r1 < m;
+            const bool pr0 = a0 && !ch0, pr1 = a1 && !ch1;
+            const bool kp0 = v0 && !a0, kp1 = v1 && !a1;
+            const unsigned bp0 = __ballot_sync(FULL, pr0), bp1 = __ballot_sync(FULL, pr1);
+            const unsigned bc0 = __ballot_sync(FULL, ch0), bc1 = __ballot_sync(FULL, ch1);
+            const unsigned bk0 = __ballot_sync(FULL, kp0), bk1 = __ballot_sync(FULL, kp1);
             __syncwarp();
-            if (prop) wl[nk + __popc(ba & lt)] = (uint16_t)i;
-            if (cher) wl[nint2 - 1 - (nc + __popc(bc & lt))] = (uint16_t)i;
-            if (valid && !act) U[nu + __popc(bk & lt)] = (uint16_t)i;
-            nk += __popc(ba);
-            nc += __popc(bc);
-            nu += __popc(bk);
+            if (pr0) wl[nk + __popc(bp0 & lt)] = (uint16_t)i0;
+            if (pr1) wl[nk + __popc(bp0) + __popc(bp1 & lt)] = (uint16_t)i1;
+            if (ch0) wl[nint2 - 1 - (nc + __popc(bc0 & lt))] = (uint16_t)i0;
+            if (ch1) wl[nint2 - 1 - (nc + __popc(bc0) + __popc(bc1 & lt))] = (uint16_t)i1;
+            if (kp0) U[nu + __popc(bk0 & lt)] = (uint16_t)i0;
+            if (kp1) U[nu + __popc(bk0) + __popc(bk1 & lt)] = (uint16_t)i1;
+            nk += __popc(bp0) + __popc(bp1);
+            nc += __popc(bc0) + __popc(bc1);
+            nu += __popc(bk0) + __popc(bk1);
           }
           nU = nu;
           if (nk + nc == 0) break;
           cnt.steps++;
           __syncwarp();
+          // active nodes whose children are both leaves make no proposal: they only become visited
           for (int j = lane; j < nc; j += 32) {
-            pri[wl[nint2 - 1 - j]] = 0;
+            key[wl[nint2 - 1 - j]] = 0u;
             cnt.visits++;
           }
           for (int j = lane; j < nk; j += 32) {
             int i = wl[j];
             visit<NW, true>(X_, lab, ch, cz, S, par, m + i, sw, chain, cnt);
-            pri[i] = 0;
+            key[i] = 0u;
             cnt.visits++;
           }
           cnt.busy += nk;
@@ -605,7 +605,9 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
 
 // ================================================================================================
 // k_anneal_pair<NW>: par order with two warps per chain (64 lanes), so that twice as many warps are
-// resident for the same shared memory; registers are capped for 14 pairs per SM.  Same chain slot as
+// resident for the same shared memory; registers are capped for 14 pairs per SM.  Measured on C2 it is
+// 7 % slower than one warp per chain (barrier and atomic overheads outweigh the occupancy), so the plan
+// uses it only when asked (kernel_hint 3).  Same chain slot as
 // k_anneal_warp plus a second unvisited list: the phase scan compacts with shared-memory atomics
 // (entries land in any order; the moves of one phase commute), and the two warps meet at a named
 // barrier after the scan and after the visits of every phase.
@@ -1444,7 +1446,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   if (e != cudaSuccess) return e;
   bool warp_ok = (L.nw == 1 || L.nw == 2 || L.nw == 4 || L.nw == 6 || L.nw == 8) && hint != 2;
   // par order: two warps per chain (up to 14 pairs per SM)
-  if (warp_ok && order == 0 && (hint == 0 || hint == 3)) {
+  if (warp_ok && order == 0 && hint == 3) {
     int np = 14;
     while (np > 0 && PairSmem::make(L, np, slice_moves).total > (uint32_t)optin) np--;
     if (np > 0) {
@@ -1464,7 +1466,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   if (warp_ok) {
     // as many chain slots per CTA as fit (at most 16 warps), one CTA per SM
     int wpc = 16;
-    while (wpc > 0 && WarpSmem::make(L, wpc).total > (uint32_t)optin) wpc--;
+    while (wpc > 0 && WarpSmem::make(L, wpc, slice_moves).total > (uint32_t)optin) wpc--;
     if (wpc > 0) {
       int need = (nchains + wpc - 1) / wpc;
       // fewer chains than slots: spread them over more CTAs with fewer warps each
@@ -1475,7 +1477,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
       plan->kind = K_WARP;
       plan->warps_per_cta = wpc;
       plan->grid = need < nsm ? need : nsm;
-      plan->smem = WarpSmem::make(L, wpc).total;
+      plan->smem = WarpSmem::make(L, wpc, slice_moves).total;
       return cudaSuccess;
     }
   }

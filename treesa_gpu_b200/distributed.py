@@ -16,12 +16,19 @@ import os
 from . import driver, engine
 
 
+_IDS = {}
+
+
 def nccl_id_for_group(group=None):
-    """A fresh ncclUniqueId created on rank 0 and broadcast over the torch.distributed group."""
+    """The ncclUniqueId of this process group: created on rank 0 and broadcast once; later calls reuse it
+    and with it the library's cached NCCL communicator."""
     import torch.distributed as dist
-    obj = [engine.nccl_unique_id() if dist.get_rank(group) == 0 else None]
-    dist.broadcast_object_list(obj, src=0, group=group)
-    return obj[0]
+    key = id(group) if group is not None else "world"
+    if key not in _IDS:
+        obj = [engine.nccl_unique_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        _IDS[key] = obj[0]
+    return _IDS[key]
 
 
 def optimize_distributed(ixs, iy, group=None, device=None, **kw):

@@ -131,6 +131,15 @@ class Session:
             pass
 
 
+def resample(records_ptr, anc, rec_bytes, stream=None):
+    """tsa_resample: device records (pointer, nchains x rec_bytes) <- their ancestors, in place."""
+    anc = np.ascontiguousarray(anc, np.int32)
+    err = C.create_string_buffer(512)
+    rc = _abi.lib().tsa_resample(C.c_void_p(records_ptr), anc.ctypes.data_as(C.POINTER(C.c_int32)), len(anc),
+                                 int(rec_bytes), stream, err, 512)
+    _abi.check(rc, err, "tsa_resample")
+
+
 def nccl_unique_id():
     """128-byte ncclUniqueId for a multi-GPU run (rank 0 creates it and shares it)."""
     buf = C.create_string_buffer(128)
