@@ -157,6 +157,17 @@ int tsa_session_stats(tsa_session* s, uint64_t* counters12, double* kernel_secon
 int tsa_resample(void* records, const int32_t* anc, int32_t nchains, uint32_t rec_bytes, void* stream, char* err,
                  size_t errlen);
 
+/* tsa_resample without any allocation, for callers that cannot allocate device memory when they
+ * resample: a host thread capturing a CUDA graph, a process whose device memory belongs to its own fixed
+ * pool, or a loop where cudaMalloc/cudaFree would synchronize the device.  Same arguments and result as
+ * tsa_resample; the scratch is a static device array built into the library (64 MiB of records and
+ * 65536 ancestor slots, held by every GPU that loads it until exit), so at most 65536 chains and 64 MiB
+ * of records; larger populations are rejected with TSA_ERR_ARG.  The first call on a device (with that
+ * device current) looks the array up; make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race.  No counterpart in the reference. */
+int tsa_resample_noalloc(void* records, const int32_t* anc, int32_t nchains, uint32_t rec_bytes, void* stream,
+                         char* err, size_t errlen);
+
 /* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
  * kernel (1 warp-per-chain, 2 CTA-per-chain), warps per CTA, grid, dynamic shared memory bytes}. */
 int tsa_session_info(tsa_session* s, int32_t* info8);
