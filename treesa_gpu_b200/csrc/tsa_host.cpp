@@ -438,6 +438,9 @@ struct tsa_session {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   cudaEvent_t evk[4] = {nullptr, nullptr, nullptr, nullptr};  // kernel start/end, two level parities
   cudaEvent_t eve[2] = {nullptr, nullptr};                    // energies of a level on the host
+  cudaStream_t cst = nullptr;                                 // energy gathers and best-record copies
+  cudaEvent_t evdone[2] = {nullptr, nullptr};                 // a level's kernel has finished (on st)
+  cudaEvent_t evfree[2] = {nullptr, nullptr};                 // cst is done with a level's buffers
   float* h_lc = nullptr;                                      // pinned [2][nglobal]
   int *h_sc = nullptr, *h_ns = nullptr;
   uint8_t* h_best = nullptr;                                  // pinned best record
@@ -478,6 +481,11 @@ struct tsa_session {
       if (e) cudaEventDestroy(e);
     for (auto& e : eve)
       if (e) cudaEventDestroy(e);
+    for (auto& e : evdone)
+      if (e) cudaEventDestroy(e);
+    for (auto& e : evfree)
+      if (e) cudaEventDestroy(e);
+    if (cst) cudaStreamDestroy(cst);
     cudaFreeHost(h_lc);
     cudaFreeHost(h_sc);
     cudaFreeHost(h_ns);
@@ -530,6 +538,9 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
   CKR(cudaMallocHost(&s->h_best, s->L.rec_bytes));
   for (auto& e : s->evk) CKR(cudaEventCreate(&e));
   for (auto& e : s->eve) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (auto& e : s->evdone) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (auto& e : s->evfree) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  CKR(cudaStreamCreateWithFlags(&s->cst, cudaStreamNonBlocking));
   CKR(cudaMalloc(&s->d_anc, s->nchains * sizeof(int)));
   CKR(cudaMalloc(&s->d_err, sizeof(int)));
   CKR(cudaMalloc(&s->d_stats, 10 * sizeof(unsigned long long)));
@@ -838,26 +849,26 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       fprintf(stderr, "lev %4zu beta %7.3f  best(l2cost/slice %.3f sc %d |S| %d)  meanE %.3f  families %d  t=%.2fs\n",
               lev, s->betas[lev], (double)glc[bi], gsc[bi], gns[bi], meanE, nf, now_s() - t0);
   };
-  // enqueue: energies of this level (all ranks) into pinned host slot q
-  auto gather = [&](int q) -> int {
+  // enqueue on stream cs: energies of this level (all ranks) into pinned host slot q
+  auto gather = [&](int q, cudaStream_t cs) -> int {
     if (s->world > 1)
       return s->comm->allgather_energies(s->d_lc + (size_t)q * nch, s->d_sc + (size_t)q * nch,
                                          s->d_ns + (size_t)q * nch, nch, s->h_lc + (size_t)q * ng,
-                                         s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, s->st, err, errlen);
+                                         s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, cs, err, errlen);
     CKR(cudaMemcpyAsync(s->h_lc + (size_t)q * ng, s->d_lc + (size_t)q * nch, nch * sizeof(float),
-                        cudaMemcpyDeviceToHost, s->st));
+                        cudaMemcpyDeviceToHost, cs));
     CKR(cudaMemcpyAsync(s->h_sc + (size_t)q * ng, s->d_sc + (size_t)q * nch, nch * sizeof(int),
-                        cudaMemcpyDeviceToHost, s->st));
+                        cudaMemcpyDeviceToHost, cs));
     CKR(cudaMemcpyAsync(s->h_ns + (size_t)q * ng, s->d_ns + (size_t)q * nch, nch * sizeof(int),
-                        cudaMemcpyDeviceToHost, s->st));
+                        cudaMemcpyDeviceToHost, cs));
     return TSA_OK;
   };
-  // enqueue: copy global chain g's record out of buffer buf into the pinned best record
-  auto fetch_best = [&](int g, uint8_t* buf) -> int {
+  // enqueue on stream cs: copy global chain g's record out of buffer buf into the pinned best record
+  auto fetch_best = [&](int g, uint8_t* buf, cudaStream_t cs) -> int {
     s->d2h += rb;
     if (s->world > 1)
-      return s->comm->fetch_record(buf + (size_t)(g % nch) * rb, rb, g / nch, s->h_best, s->st, err, errlen);
-    CKR(cudaMemcpyAsync(s->h_best, buf + (size_t)g * rb, rb, cudaMemcpyDeviceToHost, s->st));
+      return s->comm->fetch_record(buf + (size_t)(g % nch) * rb, rb, g / nch, s->h_best, cs, err, errlen);
+    CKR(cudaMemcpyAsync(s->h_best, buf + (size_t)g * rb, rb, cudaMemcpyDeviceToHost, cs));
     return TSA_OK;
   };
   auto check_err = [&]() -> int {
@@ -889,9 +900,12 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         a.out_lc = s->d_lc + (size_t)q * nch;
         a.out_sc = s->d_sc + (size_t)q * nch;
         a.out_ns = s->d_ns + (size_t)q * nch;
+        // level lev-2's energies and output records (this level's slot q) must be off the device first
+        if (lev >= 2) CKR(cudaStreamWaitEvent(s->st, s->evfree[q], 0));
         CKR(cudaEventRecord(s->evk[2 * q], s->st));
         CKR(tsa::launch_sweeps(a, s->plan, s->st));
         CKR(cudaEventRecord(s->evk[2 * q + 1], s->st));
+        CKR(cudaEventRecord(s->evdone[q], s->st));
         s->launches++;
         s->sweep_ctr += (uint32_t)s->niters;
       }
@@ -900,19 +914,23 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         CKR(cudaEventSynchronize(s->eve[q]));
         int improved;
         process((size_t)pend, s->h_lc + (size_t)q * ng, s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, &improved);
-        if (improved >= 0) rc = fetch_best(improved, buf[q ^ 1]);  // level pend's output buffer
+        if (improved >= 0) rc = fetch_best(improved, buf[q ^ 1], s->cst);  // level pend's output buffer
+        if (rc == TSA_OK) CKR(cudaEventRecord(s->evfree[q], s->cst));
         pend = -1;
       }
       if (lev < nlev && rc == TSA_OK) {
         const int q = (int)(lev & 1);
         const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || lev + 1 == nlev;
+        CKR(cudaStreamWaitEvent(s->cst, s->evdone[q], 0));
         if (eval) {
-          rc = gather(q);
+          rc = gather(q, s->cst);
           if (rc == TSA_OK) {
-            CKR(cudaEventRecord(s->eve[q], s->st));
+            CKR(cudaEventRecord(s->eve[q], s->cst));
             s->d2h += (size_t)nch * 12;
             pend = (long)lev;
           }
+        } else {
+          CKR(cudaEventRecord(s->evfree[q], s->cst));
         }
       }
     }
@@ -942,7 +960,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       const bool last = lev + 1 == nlev;
       const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || last;
       if (eval) {
-        rc = gather(0);
+        rc = gather(0, s->st);
         if (rc) break;
         s->d2h += (size_t)nch * 12;
       }
@@ -957,7 +975,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       int improved;
       process(lev, glc, gsc, gns, &improved);
       if (improved >= 0) {
-        if ((rc = fetch_best(improved, s->d_cur))) break;
+        if ((rc = fetch_best(improved, s->d_cur, s->st))) break;
         CKR(cudaStreamSynchronize(s->st));
       }
       if (last || s->scheme == TSA_SCHEME_INDEP) continue;
@@ -1008,6 +1026,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   }
   if (rc) return rc;
   CKR(cudaStreamSynchronize(s->st));
+  CKR(cudaStreamSynchronize(s->cst));
   if ((rc = check_err())) return rc;
   memcpy(s->best.data(), s->h_best, rb);
   // the energies of the last level, this rank's chains

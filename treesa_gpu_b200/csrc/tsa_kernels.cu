@@ -217,6 +217,76 @@ __device__ __forceinline__ uint32_t visit(const WarpCtx& X_, uint64_t* lab, uint
   return chv;
 }
 
+// The same proposal split in two halves, so that a lane can evaluate two nodes of one par phase before
+// it writes either: propose() only reads, apply() writes.  Within a phase the reads of one proposal and
+// the writes of another never touch the same word (the nodes are pairwise non-adjacent, and a move at v
+// writes only v, its pivot child and the parents of O and M), so interleaving them changes nothing.
+template <int NW>
+struct Prop {
+  Set<NW> X;
+  uint32_t nchv, nchp;
+  int i, Pn, On, Mn, cP1, sx, cV1, sd;
+  bool acc;
+};
+template <int NW>
+__device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* lab, const uint32_t* ch,
+                                            const uint32_t* cz, const uint64_t* S, int v, uint32_t sweep,
+                                            uint32_t chain) {
+  const int m = X_.m;
+  Prop<NW> p;
+  p.i = v - m;
+  uint32_t chv = ch[p.i];
+  int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
+  bool li = l >= m, ri = r >= m;
+  U4 rnd = philox10((uint32_t)v, sweep, chain, 0u, X_.key0, X_.key1);
+  int rule = pick_rule(li, ri, rnd.x);
+  int slotP = rule >> 1;
+  int slotM = ((rule ^ (rule >> 1)) & 1) ^ 1;
+  p.Pn = slotP ? r : l;
+  p.On = slotP ? l : r;
+  uint32_t chp = ch[p.Pn - m];
+  p.Mn = slotM ? (int)(chp >> 16) : (int)(chp & 0xFFFFu);
+  int Kn = slotM ? (int)(chp & 0xFFFFu) : (int)(chp >> 16);
+  const uint64_t* pO = p.On >= m ? lab + (size_t)(p.On - m) * NW : X_.leaf + (size_t)p.On * NW;
+  const uint64_t* pK = Kn >= m ? lab + (size_t)(Kn - m) * NW : X_.leaf + (size_t)Kn * NW;
+  const uint64_t* pM = p.Mn >= m ? lab + (size_t)(p.Mn - m) * NW : X_.leaf + (size_t)p.Mn * NW;
+  Set<NW> D = ldset<NW>(lab + (size_t)p.i * NW), O = ldset<NW>(pO), K = ldset<NW>(pK), M = ldset<NW>(pM);
+  int sx = 0, k2 = 0, k3 = 0;
+#pragma unroll
+  for (int w = 0; w < NW; w++) {
+    uint64_t nm = X_.slicing ? ~S[w] : ~0ull;
+    uint64_t x = (K.w[w] | O.w[w]) & (M.w[w] | D.w[w]);
+    p.X.w[w] = x;
+    uint64_t xm = x & nm;
+    sx += __popcll(xm);
+    k2 += __popcll(K.w[w] & O.w[w] & ~x & nm);
+    k3 += __popcll(xm & M.w[w] & ~D.w[w]);
+  }
+  uint32_t czv = cz[p.i], czp = cz[p.Pn - m];
+  p.sd = (int)(czv & 0xFFFFu);
+  int sp = (int)(czp & 0xFFFFu);
+  p.sx = sx;
+  p.cP1 = sx + k2;
+  p.cV1 = p.sd + k3;
+  float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, p.sd, sx, p.cP1, p.cV1, X_.sc_target, X_.sc_weight,
+                         X_.lse);
+  p.acc = accept(X_, rnd.y, dE);
+  p.nchp = slotM ? ((chp & 0xFFFFu) | ((uint32_t)p.On << 16)) : ((chp & 0xFFFF0000u) | (uint32_t)p.On);
+  p.nchv = slotP ? ((chv & 0xFFFF0000u) | (uint32_t)p.Mn) : ((chv & 0xFFFFu) | ((uint32_t)p.Mn << 16));
+  return p;
+}
+template <int NW>
+__device__ __forceinline__ void apply(const Prop<NW>& p, int m, uint64_t* lab, uint32_t* ch, uint32_t* cz,
+                                      uint16_t* par) {
+  stset<NW>(lab + (size_t)(p.Pn - m) * NW, p.X);
+  cz[p.Pn - m] = ((uint32_t)p.cP1 << 16) | (uint32_t)p.sx;
+  cz[p.i] = ((uint32_t)p.cV1 << 16) | (uint32_t)p.sd;
+  ch[p.Pn - m] = p.nchp;
+  ch[p.i] = p.nchv;
+  if (p.On >= m) par[p.On - m] = (uint16_t)p.Pn;
+  if (p.Mn >= m) par[p.Mn - m] = (uint16_t)(m + p.i);
+}
+
 // float log2(2^a + 2^b) with the device's log2f/exp2f, exactly the reference's lse_f (common.h:121-126)
 __device__ __forceinline__ float lse_f(float a, float b) {
   float mx = a > b ? a : b;
@@ -516,8 +586,24 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
             key[wl[nint2 - 1 - j]] = 0u;
             cnt.visits++;
           }
-          for (int j = lane; j < nk; j += 32) {
-            int i = wl[j];
+          // more than 32 proposals: two per lane, both evaluated before either is applied
+          int j = lane;
+          for (; nk - (j - lane) > 32; j += 64) {
+            const int ja = j, jb = j + 32;
+            const bool vb = jb < nk;
+            const int ia = wl[ja], ib = vb ? (int)wl[jb] : ia;
+            Prop<NW> pa = propose<NW>(X_, lab, ch, cz, S, m + ia, sw, chain);
+            Prop<NW> pb = propose<NW>(X_, lab, ch, cz, S, m + ib, sw, chain);
+            cnt.prop += 1 + vb;
+            cnt.acc += pa.acc + (vb && pb.acc);
+            cnt.visits += 1 + vb;
+            if (pa.acc) apply<NW>(pa, m, lab, ch, cz, par);
+            if (vb && pb.acc) apply<NW>(pb, m, lab, ch, cz, par);
+            key[ia] = 0u;
+            if (vb) key[ib] = 0u;
+          }
+          if (j < nk) {
+            const int i = wl[j];
             visit<NW, true>(X_, lab, ch, cz, S, par, m + i, sw, chain, cnt);
             key[i] = 0u;
             cnt.visits++;
