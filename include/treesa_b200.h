@@ -86,8 +86,9 @@ typedef struct tsa_options {
                                  csrc/cpu_ref.h, default); 1 = the device's expf (bit-exact with the
                                  reference's GPU binary, csrc/common.h:228 compiled by nvcc) */
   int32_t kernel_hint;        /* 0 auto; 1 one warp per chain (chain in shared memory); 2 one CTA per chain
-                                 (label sets in HBM); 3 two warps per chain (par order).  Never changes a
-                                 result. */
+                                 (label sets in HBM); 3 two warps per chain (par order); 4 a cluster of two
+                                 CTAs per chain (par order, chunk summaries, no slice moves).  Never changes
+                                 a result. */
   int32_t reserved[12];
 } tsa_options;
 
@@ -169,7 +170,8 @@ int tsa_resample_noalloc(void* records, const int32_t* anc, int32_t nchains, uin
                          char* err, size_t errlen);
 
 /* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
- * kernel (1 warp-per-chain, 2 CTA-per-chain), warps per CTA, grid, dynamic shared memory bytes}. */
+ * kernel (1 warp per chain, 2 CTA per chain, 3 two warps per chain, 4 two CTAs per chain), warps per CTA,
+ * grid, dynamic shared memory bytes}. */
 int tsa_session_info(tsa_session* s, int32_t* info8);
 
 /* Energies of every chain after the last evaluated level (lcost per slice, sc, |S|), for tests. */

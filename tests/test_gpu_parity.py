@@ -44,11 +44,13 @@ def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None, kerne
 WIDE = ["grid24", "grid28", "sq46"]  # 576, 784 and 4140 labels: CTA-per-chain kernel (sq46 with summaries)
 
 
-@pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
+@pytest.mark.parametrize("kernel", ["warp", "pair", "block", "cta_pair"])
 @pytest.mark.parametrize("order", ["par", "preorder"])
 @pytest.mark.parametrize("name", SMALL + WIDE)
 def test_trajectories_bit_exact(name, order, kernel):
-    if name in WIDE and kernel != "block":
+    if kernel == "cta_pair" and (name != "sq46" or order != "par"):
+        pytest.skip("a CTA pair per chain is the par-order kernel for label sets with chunk summaries")
+    if name in WIDE and kernel not in ("block", "cta_pair"):
         pytest.skip("wide label sets have no shared-memory layout")
     if kernel == "pair" and order == "preorder":
         pytest.skip("two warps per chain is the par-order kernel")
@@ -135,11 +137,12 @@ def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
 
 
 @pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
-@pytest.mark.parametrize("name", ["sat100", "reg3_250", "grid24"])
+@pytest.mark.parametrize("name", ["sat100", "reg3_250", "grid24", "sq46"])
 def test_fixed_slice_set_bit_exact(name, kernel):
-    """A fixed slice set (labels of size 1): every cost on the sliced network (reference check section C)."""
+    """A fixed slice set (labels of size 1): every cost on the sliced network (reference check section C).
+    sq46 runs the chunk-summary kernel with a slice mask."""
     rec = _util.instance(name)
-    if name == "grid24" and kernel != "block":
+    if name in WIDE and kernel != "block":
         pytest.skip("wide")
     net, onet = _net(rec)
     rng = np.random.default_rng(8)
@@ -147,10 +150,11 @@ def test_fixed_slice_set_bit_exact(name, kernel):
     S = np.zeros(onet.nw, np.uint64)
     for l in sl:
         S[l >> 6] |= np.uint64(1) << np.uint64(l & 63)
-    trees = _util.start_trees(rec, 32, seed=8)
+    nch = 16 if name in WIDE else 32
+    trees = _util.start_trees(rec, nch, seed=8)
     t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 3, "par", 8, 18.0, S=sl, kernel=kernel)
     ot, olab, ocnt = O.sweeps(onet, trees, CHECK_BETAS, 3, order="par", seed=8, sc_target=18.0,
-                              S=np.tile(S, (32, 1)))
+                              S=np.tile(S, (nch, 1)))
     assert (t == ot).all() and (lab[:, :, :onet.nw] == olab).all()
     assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
 

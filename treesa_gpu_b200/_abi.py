@@ -139,7 +139,8 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
     o.verbose = int(bool(verbose))
     o.max_levels = int(max_levels)
     o.exp_mode = {"host": 0, "device": 1}[exp_mode]
-    o.kernel_hint = {0: 0, 1: 1, 2: 2, 3: 3, "auto": 0, "warp": 1, "block": 2, "pair": 3}[kernel_hint]
+    o.kernel_hint = {0: 0, 1: 1, 2: 2, 3: 3, 4: 4, "auto": 0, "warp": 1, "block": 2, "pair": 3,
+                     "cta_pair": 4}[kernel_hint]
     return o
 
 

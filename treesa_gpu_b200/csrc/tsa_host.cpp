@@ -695,6 +695,11 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   s->max_slices = O->max_slices > 0 ? O->max_slices : I.nlab;
   s->select_sc = O->select_sc ? 1 : 0;
   s->verbose = O->verbose;
+  if (O->kernel_hint < 0 || O->kernel_hint > 4) {
+    set_err(err, errlen, "kernel_hint must be 0 (auto), 1 (warp), 2 (block), 3 (pair of warps) or 4 (pair of CTAs)");
+    delete s;
+    return TSA_ERR_ARG;
+  }
   if (O->exp_mode < 0 || O->exp_mode > 1) {
     set_err(err, errlen, "exp_mode must be 0 (host libm) or 1 (device expf)");
     delete s;
@@ -1121,7 +1126,10 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
   res->trace = (double*)malloc(sizeof(double) * std::max<size_t>(1, s->trace.size()));
   if (!s->trace.empty()) memcpy(res->trace, s->trace.data(), s->trace.size() * 8);
   snprintf(res->kernel, sizeof res->kernel, "%s",
-           s->plan.kind == tsa::K_WARP ? "warp_smem" : s->plan.kind == tsa::K_PAIR ? "pair_smem" : "block_hbm");
+           s->plan.kind == tsa::K_WARP   ? "warp_smem"
+           : s->plan.kind == tsa::K_PAIR ? "pair_smem"
+           : s->plan.cluster == 2        ? "cta_pair_hbm"
+                                         : "block_hbm");
   res->h2d_bytes = s->h2d;
   res->d2h_bytes = s->d2h;
   return valid && labels_ok ? TSA_OK : TSA_ERR_INVALID;
@@ -1195,7 +1203,7 @@ int tsa_session_info(tsa_session* s, int32_t* v) {
   v[1] = s->L.nint;
   v[2] = s->L.nw;
   v[3] = (int32_t)s->L.rec_bytes;
-  v[4] = s->plan.kind == tsa::K_WARP ? 1 : s->plan.kind == tsa::K_BLOCK ? 2 : 3;
+  v[4] = s->plan.kind == tsa::K_WARP ? 1 : s->plan.kind == tsa::K_BLOCK ? (s->plan.cluster == 2 ? 4 : 2) : 3;
   v[5] = s->plan.warps_per_cta;
   v[6] = s->plan.grid;
   v[7] = (int32_t)s->plan.smem;

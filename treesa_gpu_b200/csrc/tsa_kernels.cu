@@ -13,6 +13,7 @@
 //
 // Every kernel produces bit-identical trees to the reference's CPU port (csrc/cpu_ref.h) for the same
 // Philox counters; see tsa_core.h for the arithmetic.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -142,6 +143,20 @@ struct WarpCtx {
 struct Counters {
   unsigned long long prop, acc, steps, visits, sprop, sacc, busy, chunks, chunks_acc;
 };
+// per-chain counts of one lane (32-bit adds in the inner loops), added into Counters after each chain
+struct ChainCounters {
+  uint32_t prop, acc, steps, visits, sprop, sacc, busy;
+  __device__ __forceinline__ void flush(Counters& c) {
+    c.prop += prop;
+    c.acc += acc;
+    c.steps += steps;
+    c.visits += visits;
+    c.sprop += sprop;
+    c.sacc += sacc;
+    c.busy += busy;
+    *this = ChainCounters{};
+  }
+};
 
 // Metropolis: host-libm-exact (default) or with the device's expf as the reference's GPU binary
 __device__ __forceinline__ bool accept_rt(int exp_device, float beta, const double* exptab, uint32_t r, float dE) {
@@ -158,69 +173,12 @@ __device__ __forceinline__ bool accept(const WarpCtx& X_, uint32_t r, float dE) 
 // One TreeSA proposal at internal node v (one lane).  Semantics: csrc/cpu_ref.h:89-121 (Julia
 // optimize_subtree! at one node).  With P the pivot child (left for rules 0,1), O the other child,
 // M the pivot's child that moves up and K the one that stays, every rule swaps M and O keeping slots,
-// and P gets labels X = (K|O) & (M|D).  Returns v's children word after the move; on accept also
-// rewrites P's labels and both (cost, size) words and, for par order, the parents of O and M.
-template <int NW, bool PAR>
-__device__ __forceinline__ uint32_t visit(const WarpCtx& X_, uint64_t* lab, uint32_t* ch, uint32_t* cz,
-                                          const uint64_t* S, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
-                                          Counters& cnt) {
-  const int m = X_.m;
-  const int i = v - m;
-  uint32_t chv = ch[i];
-  int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
-  bool li = l >= m, ri = r >= m;
-  if (!li && !ri) return chv;
-  U4 rnd = philox10((uint32_t)v, sweep, chain, 0u, X_.key0, X_.key1);
-  int rule = pick_rule(li, ri, rnd.x);
-  int slotP = rule >> 1;
-  int slotM = ((rule ^ (rule >> 1)) & 1) ^ 1;
-  int Pn = slotP ? r : l, On = slotP ? l : r;
-  uint32_t chp = ch[Pn - m];
-  int Mn = slotM ? (int)(chp >> 16) : (int)(chp & 0xFFFFu);
-  int Kn = slotM ? (int)(chp & 0xFFFFu) : (int)(chp >> 16);
-  const uint64_t* pO = On >= m ? lab + (size_t)(On - m) * NW : X_.leaf + (size_t)On * NW;
-  const uint64_t* pK = Kn >= m ? lab + (size_t)(Kn - m) * NW : X_.leaf + (size_t)Kn * NW;
-  const uint64_t* pM = Mn >= m ? lab + (size_t)(Mn - m) * NW : X_.leaf + (size_t)Mn * NW;
-  Set<NW> D = ldset<NW>(lab + (size_t)i * NW), O = ldset<NW>(pO), K = ldset<NW>(pK), M = ldset<NW>(pM);
-  Set<NW> Xs;
-  int sx = 0, k2 = 0, k3 = 0;
-#pragma unroll
-  for (int w = 0; w < NW; w++) {
-    uint64_t nm = X_.slicing ? ~S[w] : ~0ull;
-    uint64_t x = (K.w[w] | O.w[w]) & (M.w[w] | D.w[w]);
-    Xs.w[w] = x;
-    uint64_t xm = x & nm;
-    sx += __popcll(xm);
-    k2 += __popcll(K.w[w] & O.w[w] & ~x & nm);
-    k3 += __popcll(xm & M.w[w] & ~D.w[w]);
-  }
-  uint32_t czv = cz[i], czp = cz[Pn - m];
-  int sd = (int)(czv & 0xFFFFu), sp = (int)(czp & 0xFFFFu);
-  int cP1 = sx + k2, cV1 = sd + k3;
-  float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, X_.sc_target, X_.sc_weight, X_.lse);
-  cnt.prop++;
-  if (accept(X_, rnd.y, dE)) {
-    cnt.acc++;
-    stset<NW>(lab + (size_t)(Pn - m) * NW, Xs);
-    cz[Pn - m] = ((uint32_t)cP1 << 16) | (uint32_t)sx;
-    cz[i] = ((uint32_t)cV1 << 16) | (uint32_t)sd;
-    uint32_t nchp = slotM ? ((chp & 0xFFFFu) | ((uint32_t)On << 16)) : ((chp & 0xFFFF0000u) | (uint32_t)On);
-    uint32_t nchv = slotP ? ((chv & 0xFFFF0000u) | (uint32_t)Mn) : ((chv & 0xFFFFu) | ((uint32_t)Mn << 16));
-    ch[Pn - m] = nchp;
-    ch[i] = nchv;
-    if (PAR) {
-      if (On >= m) par[On - m] = (uint16_t)Pn;
-      if (Mn >= m) par[Mn - m] = (uint16_t)v;
-    }
-    chv = nchv;
-  }
-  return chv;
-}
-
-// The same proposal split in two halves, so that a lane can evaluate two nodes of one par phase before
-// it writes either: propose() only reads, apply() writes.  Within a phase the reads of one proposal and
-// the writes of another never touch the same word (the nodes are pairwise non-adjacent, and a move at v
-// writes only v, its pivot child and the parents of O and M), so interleaving them changes nothing.
+// and P gets labels X = (K|O) & (M|D).  propose() only reads; apply() rewrites P's labels, both
+// (cost, size) words, both children words and, for par order, the parents of O and M.  A lane may
+// evaluate two nodes of one par phase before it writes either: within a phase the reads of one
+// proposal and the writes of another never touch the same word (the nodes are pairwise non-adjacent,
+// and a move at v writes only v, its pivot child and the parents of O and M).
+// NM holds the labels that are not sliced (all ones without slicing).
 template <int NW>
 struct Prop {
   Set<NW> X;
@@ -230,12 +188,11 @@ struct Prop {
 };
 template <int NW>
 __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* lab, const uint32_t* ch,
-                                            const uint32_t* cz, const uint64_t* S, int v, uint32_t sweep,
-                                            uint32_t chain) {
+                                            const uint32_t* cz, const Set<NW>& NM, int v, uint32_t chv,
+                                            uint32_t sweep, uint32_t chain) {
   const int m = X_.m;
   Prop<NW> p;
   p.i = v - m;
-  uint32_t chv = ch[p.i];
   int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
   bool li = l >= m, ri = r >= m;
   U4 rnd = philox10((uint32_t)v, sweep, chain, 0u, X_.key0, X_.key1);
@@ -254,12 +211,11 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
   int sx = 0, k2 = 0, k3 = 0;
 #pragma unroll
   for (int w = 0; w < NW; w++) {
-    uint64_t nm = X_.slicing ? ~S[w] : ~0ull;
     uint64_t x = (K.w[w] | O.w[w]) & (M.w[w] | D.w[w]);
     p.X.w[w] = x;
-    uint64_t xm = x & nm;
+    uint64_t xm = x & NM.w[w];
     sx += __popcll(xm);
-    k2 += __popcll(K.w[w] & O.w[w] & ~x & nm);
+    k2 += __popcll(K.w[w] & O.w[w] & ~x & NM.w[w]);
     k3 += __popcll(xm & M.w[w] & ~D.w[w]);
   }
   uint32_t czv = cz[p.i], czp = cz[p.Pn - m];
@@ -275,7 +231,7 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
   p.nchv = slotP ? ((chv & 0xFFFF0000u) | (uint32_t)p.Mn) : ((chv & 0xFFFFu) | ((uint32_t)p.Mn << 16));
   return p;
 }
-template <int NW>
+template <int NW, bool PAR>
 __device__ __forceinline__ void apply(const Prop<NW>& p, int m, uint64_t* lab, uint32_t* ch, uint32_t* cz,
                                       uint16_t* par) {
   stset<NW>(lab + (size_t)(p.Pn - m) * NW, p.X);
@@ -283,8 +239,35 @@ __device__ __forceinline__ void apply(const Prop<NW>& p, int m, uint64_t* lab, u
   cz[p.i] = ((uint32_t)p.cV1 << 16) | (uint32_t)p.sd;
   ch[p.Pn - m] = p.nchp;
   ch[p.i] = p.nchv;
-  if (p.On >= m) par[p.On - m] = (uint16_t)p.Pn;
-  if (p.Mn >= m) par[p.Mn - m] = (uint16_t)(m + p.i);
+  if (PAR) {
+    if (p.On >= m) par[p.On - m] = (uint16_t)p.Pn;
+    if (p.Mn >= m) par[p.Mn - m] = (uint16_t)(m + p.i);
+  }
+}
+// propose + apply at one node; returns v's children word after the move (unchanged for a leaf-only node)
+template <int NW, bool PAR, typename C>
+__device__ __forceinline__ uint32_t visit(const WarpCtx& X_, uint64_t* lab, uint32_t* ch, uint32_t* cz,
+                                          const Set<NW>& NM, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
+                                          C& cnt) {
+  const uint32_t chv = ch[v - X_.m];
+  if ((int)(chv & 0xFFFFu) < X_.m && (int)(chv >> 16) < X_.m) return chv;
+  Prop<NW> p = propose<NW>(X_, lab, ch, cz, NM, v, chv, sweep, chain);
+  cnt.prop++;
+  if (p.acc) {
+    cnt.acc++;
+    apply<NW, PAR>(p, X_.m, lab, ch, cz, par);
+    return p.nchv;
+  }
+  return chv;
+}
+
+// Not-sliced label mask of a chain in registers
+template <int NW>
+__device__ __forceinline__ Set<NW> not_sliced(const uint64_t* S, int slicing) {
+  Set<NW> nm;
+#pragma unroll
+  for (int w = 0; w < NW; w++) nm.w[w] = slicing ? ~S[w] : ~0ull;
+  return nm;
 }
 
 // float log2(2^a + 2^b) with the device's log2f/exp2f, exactly the reference's lse_f (common.h:121-126)
@@ -390,9 +373,9 @@ __device__ __forceinline__ int nth_label(const uint64_t* A, const uint64_t* S, i
 
 // Slice moves of one chain (warp-cooperative): slice_step, csrc/treesa_gpu.cu:445-502.  Costs of the
 // proposed slice set are computed into the scratch cache cz2 and committed on accept.
-template <int NW>
+template <int NW, typename C>
 __device__ void slice_step(const WarpCtx& X_, const SweepArgs& a, uint64_t* lab, uint32_t* ch, uint32_t* cz,
-                           uint32_t* cz2, uint64_t* S, uint32_t sweep, uint32_t chain, int lane, Counters& cnt) {
+                           uint32_t* cz2, uint64_t* S, uint32_t sweep, uint32_t chain, int lane, C& cnt) {
   EvalOut cur = eval_cached<NW>(X_, cz, S, a.leaf_sc, lane);
   float Ecur = slice_energy(cur, X_.sc_target, X_.sc_weight);
   for (int j = 0; j < a.slice_moves; j++) {
@@ -499,7 +482,8 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   const int m = L.m, nint = L.nint, nint2 = W.nint2;
   const unsigned FULL = 0xFFFFFFFFu;
   const unsigned lt = (1u << lane) - 1u;
-  Counters cnt{};
+  Counters tot{};
+  ChainCounters cnt{};
   uint32_t phase = 0;
   bool failed = false;
 
@@ -530,6 +514,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
       if (lane == 0) par[nint - 1] = 0xFFFFu;
       __syncwarp();
     }
+    Set<NW> NM = not_sliced<NW>(S, X_.slicing);
     for (int s = 0; s < a.nsweeps; s++) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
       if (ORDER == 0) {
@@ -592,19 +577,20 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
             const int ja = j, jb = j + 32;
             const bool vb = jb < nk;
             const int ia = wl[ja], ib = vb ? (int)wl[jb] : ia;
-            Prop<NW> pa = propose<NW>(X_, lab, ch, cz, S, m + ia, sw, chain);
-            Prop<NW> pb = propose<NW>(X_, lab, ch, cz, S, m + ib, sw, chain);
+            const uint32_t cha = ch[ia], chb = ch[ib];
+            Prop<NW> pa = propose<NW>(X_, lab, ch, cz, NM, m + ia, cha, sw, chain);
+            Prop<NW> pb = propose<NW>(X_, lab, ch, cz, NM, m + ib, chb, sw, chain);
             cnt.prop += 1 + vb;
             cnt.acc += pa.acc + (vb && pb.acc);
             cnt.visits += 1 + vb;
-            if (pa.acc) apply<NW>(pa, m, lab, ch, cz, par);
-            if (vb && pb.acc) apply<NW>(pb, m, lab, ch, cz, par);
+            if (pa.acc) apply<NW, true>(pa, m, lab, ch, cz, par);
+            if (vb && pb.acc) apply<NW, true>(pb, m, lab, ch, cz, par);
             key[ia] = 0u;
             if (vb) key[ib] = 0u;
           }
           if (j < nk) {
             const int i = wl[j];
-            visit<NW, true>(X_, lab, ch, cz, S, par, m + i, sw, chain, cnt);
+            visit<NW, true>(X_, lab, ch, cz, NM, par, m + i, sw, chain, cnt);
             key[i] = 0u;
             cnt.visits++;
           }
@@ -621,7 +607,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
           int v = lane < k ? m + (int)wl[b0 + lane] : 0;
           __syncwarp();
           uint32_t cw = 0;
-          if (lane < k) cw = visit<NW, false>(X_, lab, ch, cz, S, par, v, sw, chain, cnt);
+          if (lane < k) cw = visit<NW, false>(X_, lab, ch, cz, NM, par, v, sw, chain, cnt);
           // internal children with two leaf children are visited here and now (an empty visit)
           bool c1 = lane < k && (int)(cw & 0xFFFFu) >= m;
           bool c2 = lane < k && (int)(cw >> 16) >= m;
@@ -653,9 +639,11 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
       if (a.slice_moves > 0 && (sw + 1) % (uint32_t)a.slice_every == 0) {
         __syncwarp();
         slice_step<NW>(X_, a, lab, ch, cz, cz2, S, sw, chain, lane, cnt);
+        NM = not_sliced<NW>(S, X_.slicing);
       }
       __syncwarp();
     }
+    cnt.flush(tot);
     // ---- energy of the chain after this launch (fused k_energy) ----
     EvalOut e = eval_cached<NW>(X_, cz, S, a.leaf_sc, lane);
     if (lane == 0) {
@@ -673,7 +661,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   }
   if (lane == 0) bulk_wait_all();
   // proposals, accepts and visits are per lane; phases, slice moves and busy lanes are warp-uniform
-  unsigned long long v[7] = {cnt.prop, cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc, cnt.busy};
+  unsigned long long v[7] = {tot.prop, tot.acc, tot.steps, tot.visits, tot.sprop, tot.sacc, tot.busy};
   for (int o = 16; o > 0; o >>= 1) {
     v[0] += __shfl_xor_sync(FULL, v[0], o);
     v[1] += __shfl_xor_sync(FULL, v[1], o);
@@ -809,6 +797,7 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
       uint16_t *U = Ua, *U2 = Ub;
       int nU = nint;
       psync();
+      const Set<NW> NM = not_sliced<NW>(S, X_.slicing);
       for (int ph = 0; ph <= nint; ph++) {
         int* cur = pc + 4 * (ph & 1);
         int* nxt = pc + 4 * ((ph + 1) & 1);
@@ -876,7 +865,7 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
         }
         for (int j = pl; j < nk; j += 64) {
           int i = wl[j];
-          visit<NW, true>(X_, lab, ch, cz, S, par, m + i, sw, chain, cnt);
+          visit<NW, true>(X_, lab, ch, cz, NM, par, m + i, sw, chain, cnt);
           pri[i] = 0;
           cnt.visits++;
         }
@@ -924,8 +913,14 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
 // sets stay in HBM and are streamed in 16-byte chunks by G lanes per node (the reference's visit_coop,
 // csrc/treesa_gpu.cu:267-373, with u64 words and an exact integer cost cache).
 // ================================================================================================
+// With chunk summaries, a par phase is processed as a flat list of (node, chunk) items spread evenly over
+// the CTA's threads (see par_phase_flat); these are its per-batch tables.
+constexpr int kFlatBatch = 512;   // nodes per batch (one owner thread each)
+constexpr int kFlatItems = 8192;  // (node, chunk) items per window
+
 struct BlockSmem {
   uint32_t off_ch, off_cz, off_cz2, off_sum, off_S, off_pri, off_par, off_wl, off_U, off_U2, total;
+  uint32_t off_ninfo, off_nrnd, off_ncnt, off_nxs, off_nacc, off_items, off_scan;
   int nint2;
   __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves) {
     BlockSmem b;
@@ -952,6 +947,25 @@ struct BlockSmem {
     o += 2 * n2;
     b.off_U2 = o;
     o += 2 * n2;
+    if (L.sums) {
+      o = rnd_up(o, 16);
+      b.off_ninfo = o;
+      o += 8 * kFlatBatch;
+      b.off_ncnt = o;
+      o += 8 * kFlatBatch;
+      b.off_nxs = o;
+      o += 8 * kFlatBatch;
+      b.off_nrnd = o;
+      o += 4 * kFlatBatch;
+      b.off_items = o;
+      o += 4 * kFlatItems;
+      b.off_scan = o;
+      o += 4 * 32;
+      b.off_nacc = o;
+      o += kFlatBatch;
+    } else {
+      b.off_ninfo = b.off_ncnt = b.off_nxs = b.off_nrnd = b.off_items = b.off_scan = b.off_nacc = 0;
+    }
     b.total = rnd_up(o, 128);
     return b;
   }
@@ -974,6 +988,32 @@ struct BlkCtx {
 };
 
 __device__ __forceinline__ ulonglong2 ld2(const uint64_t* p) { return *reinterpret_cast<const ulonglong2*>(p); }
+// 16-byte global load cached in L2 only: label sets that the other CTA of a cluster rewrites are never
+// read from a stale L1 line
+__device__ __forceinline__ ulonglong2 ld2_cg(const uint64_t* p) {
+  ulonglong2 r;
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];"
+               : "=l"(r.x), "=l"(r.y)
+               : "l"((unsigned long long)__cvta_generic_to_global(p))
+               : "memory");
+  return r;
+}
+// The other CTA's copies of the replicated per-node arrays of a CTA pair, each mapped with
+// map_shared_rank (distributed shared memory; null for a single CTA).  Always indexed from these bases:
+// a local shared-memory pointer plus an offset would keep the shared state space and miss the peer.
+struct PeerArrays {
+  uint32_t* ch;
+  uint32_t* cz;
+  uint64_t* sum;
+  uint16_t* par;
+  uint16_t* pri;
+};
+// element i of a replicated array in this CTA and, for a CTA pair, in the other CTA
+template <typename T>
+__device__ __forceinline__ void mset(T* local, T* peer, int i, T v) {
+  local[i] = v;
+  if (peer) peer[i] = v;
+}
 
 // lanes t, t+G, ... of the set chunks of u (SUMS) or of all chunks
 template <bool SUMS, typename F>
@@ -1232,6 +1272,229 @@ __device__ __forceinline__ int pick_group(int k, int T) {
   return G;
 }
 
+// ------------------------------------------------------------------------------------------------
+// One par phase of a chain with chunk summaries, as a flat list of (node, chunk) items.
+//
+// The label sets of a move touch a data-dependent number of 16-byte chunks (from one to the whole set),
+// so handing each node to a fixed group of lanes leaves the phase waiting for its widest node, one
+// dependent HBM/L2 round trip per chunk.  Here the phase's nodes are taken in batches of kFlatBatch:
+//   1. one owner thread per node draws the rule (Philox), finds P, O, K, M and the chunk union u;
+//   2. a block-wide exclusive scan of popc(u) numbers the batch's chunk items;
+//   3. every thread takes items e = tid, tid + T, ... (two at a time, all eight 16-byte loads issued
+//      before any is used) and adds the item's popcounts (sx, |K&O&~X|, |X&M&~D|, packed into one u64)
+//      and the nonzero bit of X into the node's shared-memory totals;
+//   4. the owner evaluates dE and the Metropolis test and rewrites the node's metadata on accept;
+//   5. the items of accepted nodes are recomputed (their sets are unchanged by the phase) and X is
+//      stored into P's chunks.
+// Same moves, same random numbers and the same integer counts as visit_coop, so the chains are
+// bit-identical; only the schedule of the loads changes.
+// ------------------------------------------------------------------------------------------------
+struct FlatTabs {
+  uint2* info;    // [batch] Pn | On << 16, Kn | Mn << 16 (x = ~0: leaf-only node)
+  uint32_t* rnd;  // [batch] Philox .y of the proposal
+  uint2* cnt;     // [batch] counts: x = sx | k2 << 16, y = k3 (each at most 64 * 128)
+  uint2* xs;      // [batch] chunk summary of X: x = chunks 0-31, y = chunks 32-63
+  uint8_t* acc;   // [batch] accepted
+  uint32_t* items;  // [window] node << 16 | chunk
+  int* scan;      // [32] per-warp totals
+};
+
+// Pass 0 returns the item's counts (sx | k2 << 16, k3) and its nonzero bit of X; pass 1 stores X.
+struct ItemCounts {
+  uint32_t a, b, xlo, xhi;
+};
+template <int PASS, int CL>
+__device__ __forceinline__ ItemCounts flat_item(const BlkCtx& B, const FlatTabs& F, const uint16_t* wlb, uint32_t it) {
+  const int m = B.m, nw = B.nw;
+  const int j = (int)(it >> 16), c = (int)(it & 0xFFFFu);
+  if (PASS == 1 && !F.acc[j]) return ItemCounts{};
+  const uint2 inf = F.info[j];
+  const int Pn = (int)(inf.x & 0xFFFFu), On = (int)(inf.x >> 16), Kn = (int)(inf.y & 0xFFFFu),
+            Mn = (int)(inf.y >> 16);
+  const int q = wlb[j];
+  auto ptr = [&](int n) { return n >= m ? B.lab + (size_t)(n - m) * nw : B.leaf + (size_t)n * nw; };
+  const uint64_t* gD = B.lab + (size_t)q * nw + 2 * c;
+  auto L2 = [](const uint64_t* p) { return CL == 1 ? ld2(p) : ld2_cg(p); };
+  const ulonglong2 d = L2(gD), o = L2(ptr(On) + 2 * c), k = L2(ptr(Kn) + 2 * c), mm = L2(ptr(Mn) + 2 * c);
+  const uint64_t x0 = (k.x | o.x) & (mm.x | d.x), x1 = (k.y | o.y) & (mm.y | d.y);
+  if (PASS == 1) {
+    *reinterpret_cast<ulonglong2*>(B.lab + (size_t)(Pn - m) * nw + 2 * c) = make_ulonglong2(x0, x1);
+    return ItemCounts{};
+  }
+  uint64_t n0 = ~0ull, n1 = ~0ull;
+  if (B.slicing) {
+    n0 = ~B.S[2 * c];
+    n1 = ~B.S[2 * c + 1];
+  }
+  const uint64_t xm0 = x0 & n0, xm1 = x1 & n1;
+  const uint32_t sx = (uint32_t)(__popcll(xm0) + __popcll(xm1));
+  const uint32_t k2 = (uint32_t)(__popcll(k.x & o.x & ~x0 & n0) + __popcll(k.y & o.y & ~x1 & n1));
+  const uint32_t k3 = (uint32_t)(__popcll(xm0 & mm.x & ~d.x) + __popcll(xm1 & mm.y & ~d.y));
+  const uint32_t nz = (x0 | x1) ? 1u : 0u;
+  return ItemCounts{sx | (k2 << 16), k3, c < 32 ? nz << c : 0u, c >= 32 ? nz << (c - 32) : 0u};
+}
+
+// Add one item per lane into its node's totals: the lanes of a node (adjacent items) are found with
+// match.any and reduced with redux.sync, so each node takes one shared-memory atomic per warp.
+__device__ __forceinline__ void flat_add(const FlatTabs& F, int j, const ItemCounts& v) {
+  const unsigned peers = __match_any_sync(0xFFFFFFFFu, j);
+  const uint32_t a = __reduce_add_sync(peers, v.a), b = __reduce_add_sync(peers, v.b);
+  const uint32_t xlo = __reduce_or_sync(peers, v.xlo), xhi = __reduce_or_sync(peers, v.xhi);
+  if (j >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1) {
+    atomicAdd(&F.cnt[j].x, a);
+    atomicAdd(&F.cnt[j].y, b);
+    if (xlo) atomicOr(&F.xs[j].x, xlo);
+    if (xhi) atomicOr(&F.xs[j].y, xhi);
+  }
+}
+
+// CL = 2: one CTA of a pair; metadata writes go to both CTAs' copies (P: the other CTA's arrays).
+template <bool PAR, int CL>
+__device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl, uint16_t* pri, uint16_t* par,
+                               int nk, uint32_t sweep, uint32_t chain, Counters& cnt, const PeerArrays& P) {
+  const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31, warp = tid >> 5, nwarps = T >> 5;
+  const int m = B.m;
+  const int NB = min(kFlatBatch, T);  // owners are threads 0..NB-1
+  for (int b0 = 0; b0 < nk; b0 += NB) {
+    const int nb = min(NB, nk - b0);
+    const uint16_t* wlb = wl + b0;
+    // 1. owners: rule, pivot and chunk union
+    int q = 0, nck = 0;
+    bool prop = false;
+    uint64_t u = 0;
+    uint32_t chv = 0;
+    if (tid < nb) {
+      q = wlb[tid];
+      chv = B.ch[q];
+      const int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
+      const bool li = l >= m, ri = r >= m;
+      prop = li || ri;
+      uint2 inf = make_uint2(0xFFFFFFFFu, 0xFFFFFFFFu);
+      if (prop) {
+        const U4 rnd = philox10((uint32_t)(m + q), sweep, chain, 0u, B.key0, B.key1);
+        const int rule = pick_rule(li, ri, rnd.x);
+        const int slotP = rule >> 1, slotM = ((rule ^ (rule >> 1)) & 1) ^ 1;
+        const int Pn = slotP ? r : l, On = slotP ? l : r;
+        const uint32_t chp = B.ch[Pn - m];
+        const int Mn = slotM ? (int)(chp >> 16) : (int)(chp & 0xFFFFu);
+        const int Kn = slotM ? (int)(chp & 0xFFFFu) : (int)(chp >> 16);
+        auto so = [&](int n) { return n >= m ? B.sum[n - m] : B.leaf_sum[n]; };
+        u = B.sum[q] | so(On) | so(Kn) | so(Mn);
+        nck = __popcll(u);
+        inf = make_uint2((uint32_t)Pn | ((uint32_t)On << 16), (uint32_t)Kn | ((uint32_t)Mn << 16));
+        F.rnd[tid] = rnd.y;
+      }
+      F.info[tid] = inf;
+      F.cnt[tid] = make_uint2(0u, 0u);
+      F.xs[tid] = make_uint2(0u, 0u);
+    }
+    // 2. exclusive scan of the chunk counts
+    int incl = nck;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) F.scan[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int v = lane < nwarps ? F.scan[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (lane >= o) v += t;
+      }
+      F.scan[lane] = v;
+    }
+    __syncthreads();
+    const int off = incl - nck + (warp ? F.scan[warp - 1] : 0);
+    const int total = F.scan[nwarps - 1];
+    auto build = [&](int w0) {  // the items numbered [w0, w0 + kFlatItems)
+      if (nck && off < w0 + kFlatItems && off + nck > w0) {
+        uint64_t uu = u;
+        for (int k = off; uu; k++) {
+          const int c = __ffsll((long long)uu) - 1;
+          uu &= uu - 1;
+          if (k >= w0 && k < w0 + kFlatItems) F.items[k - w0] = ((uint32_t)tid << 16) | (uint32_t)c;
+        }
+      }
+    };
+    // 3. counts of every item
+    for (int w0 = 0; w0 < total; w0 += kFlatItems) {
+      if (w0) __syncthreads();  // the previous window's items are consumed
+      build(w0);
+      __syncthreads();
+      const int nwin = min(kFlatItems, total - w0);
+      // warp-uniform trip count: every lane takes part in the reductions
+      for (int e0 = warp * 32; e0 < nwin; e0 += 2 * T) {
+        const int e = e0 + lane, e1 = e + T;
+        const bool v0 = e < nwin, v1 = e1 < nwin;
+        const uint32_t i0 = v0 ? F.items[e] : 0u, i1 = v1 ? F.items[e1] : 0u;
+        const ItemCounts c0 = v0 ? flat_item<0, CL>(B, F, wlb, i0) : ItemCounts{};
+        const ItemCounts c1 = v1 ? flat_item<0, CL>(B, F, wlb, i1) : ItemCounts{};
+        flat_add(F, v0 ? (int)(i0 >> 16) : -1, c0);
+        if (e0 + T < nwin) flat_add(F, v1 ? (int)(i1 >> 16) : -1, c1);
+        cnt.busy += (unsigned long long)(v0 + v1);
+      }
+    }
+    __syncthreads();
+    // 4. owners: energy, Metropolis, metadata
+    if (tid < nb) {
+      bool acc = false;
+      if (prop) {
+        const uint2 inf = F.info[tid];
+        const int Pn = (int)(inf.x & 0xFFFFu), On = (int)(inf.x >> 16), Mn = (int)(inf.y >> 16);
+        const uint2 pk = F.cnt[tid];
+        const int sx = (int)(pk.x & 0xFFFFu), k2 = (int)(pk.x >> 16), k3 = (int)pk.y;
+        const uint32_t czv = B.cz[q], czp = B.cz[Pn - m];
+        const int sd = (int)(czv & 0xFFFFu), sp = (int)(czp & 0xFFFFu);
+        const int cP1 = sx + k2, cV1 = sd + k3;
+        const float dE =
+            move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, B.sc_target, B.sc_weight, B.lse);
+        acc = accept_rt(B.exp_device, B.beta, B.exptab, F.rnd[tid], dE);
+        cnt.prop++;
+        cnt.chunks += nck;
+        if (acc) {
+          cnt.acc++;
+          cnt.chunks_acc += nck;
+          const uint32_t chp = B.ch[Pn - m];
+          const bool slotP = Pn == (int)(chv >> 16), slotM = Mn == (int)(chp >> 16);
+          mset<uint32_t>(B.ch, P.ch, Pn - m,
+                         slotM ? ((chp & 0xFFFFu) | ((uint32_t)On << 16)) : ((chp & 0xFFFF0000u) | (uint32_t)On));
+          mset<uint32_t>(B.ch, P.ch, q,
+                         slotP ? ((chv & 0xFFFF0000u) | (uint32_t)Mn) : ((chv & 0xFFFFu) | ((uint32_t)Mn << 16)));
+          mset<uint32_t>(B.cz, P.cz, Pn - m, ((uint32_t)cP1 << 16) | (uint32_t)sx);
+          mset<uint32_t>(B.cz, P.cz, q, ((uint32_t)cV1 << 16) | (uint32_t)sd);
+          mset<uint64_t>(B.sum, P.sum, Pn - m, (uint64_t)F.xs[tid].x | ((uint64_t)F.xs[tid].y << 32));
+          if (PAR) {
+            if (On >= m) mset<uint16_t>(par, P.par, On - m, (uint16_t)Pn);
+            if (Mn >= m) mset<uint16_t>(par, P.par, Mn - m, (uint16_t)(m + q));
+          }
+        }
+      }
+      F.acc[tid] = acc;
+      mset<uint16_t>(pri, P.pri, q, (uint16_t)0);
+      cnt.visits++;
+    }
+    __syncthreads();
+    // 5. X into the pivots of accepted moves
+    for (int w0 = 0; w0 < total; w0 += kFlatItems) {
+      if (total > kFlatItems) {
+        __syncthreads();
+        build(w0);
+        __syncthreads();
+      }
+      const int nwin = min(kFlatItems, total - w0);
+      int e = tid;
+      for (; e + T < nwin; e += 2 * T) {
+        const uint32_t i0 = F.items[e], i1 = F.items[e + T];
+        flat_item<1, CL>(B, F, wlb, i0);
+        flat_item<1, CL>(B, F, wlb, i1);
+      }
+      if (e < nwin) flat_item<1, CL>(B, F, wlb, F.items[e]);
+    }
+    __syncthreads();
+  }
+}
+
 template <bool SUMS, int ORDER>
 __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1274,6 +1537,14 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
   const int m = L.m, nint = L.nint;
   const unsigned lt = (1u << lane) - 1u;
+  FlatTabs F;
+  F.info = reinterpret_cast<uint2*>(smem + Bm.off_ninfo);
+  F.rnd = reinterpret_cast<uint32_t*>(smem + Bm.off_nrnd);
+  F.cnt = reinterpret_cast<uint2*>(smem + Bm.off_ncnt);
+  F.xs = reinterpret_cast<uint2*>(smem + Bm.off_nxs);
+  F.acc = smem + Bm.off_nacc;
+  F.items = reinterpret_cast<uint32_t*>(smem + Bm.off_items);
+  F.scan = reinterpret_cast<int*>(smem + Bm.off_scan);
   Counters cnt{};
   __syncthreads();
   for (int c = blockIdx.x; c < a.nchains; c += gridDim.x) {
@@ -1363,19 +1634,23 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
           U2 = tmp;
           if (nk == 0) break;
           if (tid == 0) cnt.steps++;
-          const int G = pick_group(nk, T);
-          const int groups = T / G, g = tid / G, t = tid & (G - 1);
-          const unsigned gm = G == 32 ? FULL : (((1u << G) - 1u) << (lane & ~(G - 1)));
-          for (int j = g; j < nk; j += groups) {
-            int q = wl[j];
-            visit_coop<SUMS, true>(B, par, m + q, sw, chain, G, t, gm, cnt);
-            if (t == 0) {
-              pri[q] = 0;
-              cnt.visits++;
+          if constexpr (SUMS) {
+            par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{});
+          } else {
+            const int G = pick_group(nk, T);
+            const int groups = T / G, g = tid / G, t = tid & (G - 1);
+            const unsigned gm = G == 32 ? FULL : (((1u << G) - 1u) << (lane & ~(G - 1)));
+            for (int j = g; j < nk; j += groups) {
+              int q = wl[j];
+              visit_coop<SUMS, true>(B, par, m + q, sw, chain, G, t, gm, cnt);
+              if (t == 0) {
+                pri[q] = 0;
+                cnt.visits++;
+              }
+              cnt.busy++;
             }
-            cnt.busy++;
+            __syncthreads();
           }
-          __syncthreads();
         }
       } else {
         if (tid == 0) {
@@ -1461,6 +1736,209 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   }
 }
 
+// ================================================================================================
+// k_anneal_cluster: par order with chunk summaries, one chain per cluster of two CTAs on two SMs.
+// With fewer chains than SMs (the 64x64 lattice runs 72 chains on 148 SMs) a CTA per chain leaves half of
+// the GPU idle; here both CTAs of a pair hold a full copy of the chain's per-node metadata in their own
+// shared memory, and every metadata write of a visit goes to both copies (a distributed-shared-memory
+// store).  CTA r owns the nodes q with q % 2 == r: it scans them for the phase's independent set and
+// visits the active ones with par_phase_flat; label sets stay in HBM (loaded L2-only).  The two CTAs
+// meet at one cluster barrier per phase, which also exchanges their active counts; the phase sequence
+// and every move are those of k_anneal_block, so the chains are bit-identical.
+// ================================================================================================
+__global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(128) uint8_t smem[];
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const Layout L = a.L;
+  const BlockSmem Bm = BlockSmem::make(L, a.slice_moves);
+  const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31;
+  const unsigned FULL = 0xFFFFFFFFu;
+  float* s_lse = reinterpret_cast<float*>(smem);
+  double* s_exp = reinterpret_cast<double*>(smem + 256);
+  int* sh = reinterpret_cast<int*>(smem + 768);  // [0,2) scan counters, [4,6) the peer's active counts
+  for (int q = tid; q < 64; q += T) {
+    s_lse[q] = a.lse_tab[q];
+    s_exp[q] = c_exp_tab[q];
+  }
+  BlkCtx B;
+  B.m = L.m;
+  B.nint = L.nint;
+  B.nw = L.nw;
+  B.nchunks = L.nw / 2;
+  B.key0 = a.key0;
+  B.key1 = a.key1;
+  B.beta = a.beta;
+  B.sc_target = a.sc_target;
+  B.sc_weight = a.sc_weight;
+  B.slicing = a.slicing;
+  B.exp_device = a.exp_device;
+  B.lse = s_lse;
+  B.exptab = s_exp;
+  B.leaf = a.leaf;
+  B.leaf_sum = a.leaf_sum;
+  B.ch = reinterpret_cast<uint32_t*>(smem + Bm.off_ch);
+  B.cz = reinterpret_cast<uint32_t*>(smem + Bm.off_cz);
+  B.sum = reinterpret_cast<uint64_t*>(smem + Bm.off_sum);
+  B.S = reinterpret_cast<uint64_t*>(smem + Bm.off_S);
+  uint32_t* cz2 = reinterpret_cast<uint32_t*>(smem + Bm.off_cz2);
+  uint16_t* pri = reinterpret_cast<uint16_t*>(smem + Bm.off_pri);
+  uint16_t* par = reinterpret_cast<uint16_t*>(smem + Bm.off_par);
+  uint16_t* wl = reinterpret_cast<uint16_t*>(smem + Bm.off_wl);
+  uint16_t* Ua = reinterpret_cast<uint16_t*>(smem + Bm.off_U);
+  uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
+  const int m = L.m, nint = L.nint;
+  const unsigned lt = (1u << lane) - 1u;
+  FlatTabs F;
+  F.info = reinterpret_cast<uint2*>(smem + Bm.off_ninfo);
+  F.rnd = reinterpret_cast<uint32_t*>(smem + Bm.off_nrnd);
+  F.cnt = reinterpret_cast<uint2*>(smem + Bm.off_ncnt);
+  F.xs = reinterpret_cast<uint2*>(smem + Bm.off_nxs);
+  F.acc = smem + Bm.off_nacc;
+  F.items = reinterpret_cast<uint32_t*>(smem + Bm.off_items);
+  F.scan = reinterpret_cast<int*>(smem + Bm.off_scan);
+  PeerArrays P;
+  P.ch = cl.map_shared_rank(B.ch, rank ^ 1);
+  P.cz = cl.map_shared_rank(B.cz, rank ^ 1);
+  P.sum = cl.map_shared_rank(B.sum, rank ^ 1);
+  P.par = cl.map_shared_rank(par, rank ^ 1);
+  P.pri = cl.map_shared_rank(pri, rank ^ 1);
+  int* peer_sh = cl.map_shared_rank(sh, rank ^ 1);
+  Counters cnt{};
+  const int npair = (int)(gridDim.x / 2);
+  for (int c = (int)(blockIdx.x / 2); c < a.nchains; c += npair) {
+    uint8_t* grec = a.recs + (size_t)c * L.rec_bytes;
+    B.lab = reinterpret_cast<uint64_t*>(grec);
+    const uint32_t* gch = reinterpret_cast<const uint32_t*>(grec + L.off_ch);
+    const uint32_t* gcz = reinterpret_cast<const uint32_t*>(grec + L.off_cz);
+    const uint64_t* gS = reinterpret_cast<const uint64_t*>(grec + L.off_S);
+    const uint64_t* gs = reinterpret_cast<const uint64_t*>(grec + L.off_sum);
+    for (int q = tid; q < nint; q += T) {
+      const uint32_t cw = gch[q];
+      B.ch[q] = cw;
+      B.cz[q] = gcz[q];
+      B.sum[q] = gs[q];
+      const int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+      if (l >= m) par[l - m] = (uint16_t)(m + q);
+      if (r >= m) par[r - m] = (uint16_t)(m + q);
+    }
+    if (tid == 0) par[nint - 1] = 0xFFFFu;
+    for (int q = tid; q < L.nw; q += T) B.S[q] = gS[q];
+    const uint32_t chain = (uint32_t)(a.chain0 + c);
+    const uint32_t hc = chain_hash(chain, a.key0);
+    int ph = 0;  // phases of this chain: parity selects the exchange slot
+    for (int s = 0; s < a.nsweeps; s++) {
+      const uint32_t sw = a.sweep0 + (uint32_t)s;
+      const uint32_t hs = sweep_hash(sw, hc);
+      for (int q = tid; q < nint; q += T) pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
+      int nU = (nint - rank + 1) / 2;  // the nodes q = 2j + rank
+      for (int j = tid; j < nU; j += T) Ua[j] = (uint16_t)(2 * j + rank);
+      uint16_t *U = Ua, *U2 = Ub;
+      // both copies are complete (loaded or initialised) before either CTA writes into the other
+      cl.sync();
+      for (int guard = 0; guard <= nint; guard++, ph++) {
+        if (tid == 0) {
+          sh[0] = 0;
+          sh[1] = 0;
+        }
+        __syncthreads();
+        for (int base = 0; base < nU; base += T) {
+          int j = base + tid;
+          bool valid = j < nU;
+          int q = valid ? (int)U[j] : 0;
+          bool act = false;
+          if (valid) {
+            uint32_t key = ((uint32_t)pri[q] << 16) | (uint32_t)(m + q);
+            act = true;
+            int p = par[q];
+            if (p != 0xFFFF) {
+              uint32_t pp = pri[p - m];
+              if (pp && ((pp << 16) | (uint32_t)p) > key) act = false;
+            }
+            uint32_t cw = B.ch[q];
+            int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+            if (act && l >= m) {
+              uint32_t pl = pri[l - m];
+              if (pl && ((pl << 16) | (uint32_t)l) > key) act = false;
+            }
+            if (act && r >= m) {
+              uint32_t pr = pri[r - m];
+              if (pr && ((pr << 16) | (uint32_t)r) > key) act = false;
+            }
+          }
+          unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
+          int pa = 0, pk = 0;
+          if (lane == 0) {
+            if (ba) pa = atomicAdd(&sh[0], __popc(ba));
+            if (bk) pk = atomicAdd(&sh[1], __popc(bk));
+          }
+          pa = __shfl_sync(FULL, pa, 0);
+          pk = __shfl_sync(FULL, pk, 0);
+          if (act) wl[pa + __popc(ba & lt)] = (uint16_t)q;
+          if (valid && !act) U2[pk + __popc(bk & lt)] = (uint16_t)q;
+        }
+        __syncthreads();
+        const int nk = sh[0];
+        nU = sh[1];
+        uint16_t* tmp = U;
+        U = U2;
+        U2 = tmp;
+        if (nk > 0) par_phase_flat<true, 2>(B, F, wl, pri, par, nk, sw, chain, cnt, P);
+        if (tid == 0) peer_sh[4 + (ph & 1)] = nk;
+        cl.sync();
+        const int total = nk + sh[4 + (ph & 1)];
+        if (total == 0) break;
+        if (tid == 0 && rank == 0) cnt.steps++;
+      }
+      if (a.slice_moves > 0 && (sw + 1) % (uint32_t)a.slice_every == 0) {
+        // both CTAs make the same slice moves on their own copies (same data, same random numbers)
+        __syncthreads();
+        slice_step_block(B, a, cz2, sh + 8, nullptr, sw, chain, cnt);
+      }
+      __syncthreads();
+    }
+    if (rank == 0) {
+      if (tid < 32) {
+        EvalOut e = eval_cz(B.cz, nint, B.S, L.nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+        if (lane == 0) {
+          a.out_lc[c] = e.lcost;
+          a.out_sc[c] = e.sc;
+          a.out_ns[c] = e.ns;
+        }
+      }
+      uint32_t* wch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
+      uint32_t* wcz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
+      uint64_t* wS = reinterpret_cast<uint64_t*>(grec + L.off_S);
+      uint64_t* ws = reinterpret_cast<uint64_t*>(grec + L.off_sum);
+      for (int q = tid; q < nint; q += T) {
+        wch[q] = B.ch[q];
+        wcz[q] = B.cz[q];
+        ws[q] = B.sum[q];
+      }
+      for (int q = tid; q < L.nw; q += T) wS[q] = B.S[q];
+    }
+    __syncthreads();
+  }
+  // the peer may still write into this CTA's shared memory until both have left the last phase
+  cl.sync();
+  unsigned long long v[9] = {cnt.prop,  cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc,
+                             cnt.busy, cnt.chunks, cnt.chunks_acc};
+#pragma unroll
+  for (int q = 0; q < 9; q++) {
+    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(FULL, v[q], o);
+  }
+  if (lane == 0) {
+    // slice moves were counted by all 32 lanes of warp 0 of both CTAs
+    v[4] = rank == 0 ? v[4] / 32 : 0;
+    v[5] = rank == 0 ? v[5] / 32 : 0;
+    const int slot[9] = {0, 1, 2, 3, 4, 5, 6, 8, 9};
+#pragma unroll
+    for (int q = 0; q < 9; q++)
+      if (v[q]) atomicAdd(&a.stats[slot[q]], v[q]);
+  }
+}
+
 // Population resampling: dst chain c <- src chain anc[c] (reference k_copy, :1017-1022).
 __global__ void k_copy(const uint4* __restrict__ src, uint4* __restrict__ dst, const int* __restrict__ anc, int n4) {
   const uint4* s = src + (size_t)anc[blockIdx.x] * n4;
@@ -1523,6 +2001,44 @@ static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaS
   return cudaGetLastError();
 }
 
+static cudaLaunchConfig_t cluster_config(int grid, size_t smem, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(512, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+static cudaError_t launch_cluster(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
+  size_t smem = BlockSmem::make(a.L, a.slice_moves).total;
+  cudaError_t e = cudaFuncSetAttribute(k_anneal_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cluster_config(p.grid, smem, st, attr);
+  return cudaLaunchKernelEx(&cfg, k_anneal_cluster, a);
+}
+
+// Chains that a CTA-pair launch keeps resident at once (0 if the pair cannot be launched).
+static int cluster_capacity(size_t smem, int grid) {
+  if (cudaFuncSetAttribute(k_anneal_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return 0;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cluster_config(grid, smem, 0, attr);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k_anneal_cluster, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
                         LaunchPlan* plan) {
   int nsm = 0, optin = 0;
@@ -1554,12 +2070,13 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
     int wpc = 16;
     while (wpc > 0 && WarpSmem::make(L, wpc, slice_moves).total > (uint32_t)optin) wpc--;
     if (wpc > 0) {
-      int need = (nchains + wpc - 1) / wpc;
-      // fewer chains than slots: spread them over more CTAs with fewer warps each
-      while (wpc > 1 && need < nsm) {
-        wpc = (wpc + 1) / 2;
-        need = (nchains + wpc - 1) / wpc;
-      }
+      // Chains run in waves of nsm * wpc; every chain of a launch does the same number of sweeps, so the
+      // launch takes (number of waves) chain times.  Use the fewest warps per CTA that keep that number
+      // of waves: no slot idles in the last wave, and fewer warps share each SM's issue slots.
+      const long slots = (long)nsm * wpc;
+      const long waves = (nchains + slots - 1) / slots;
+      wpc = (int)((nchains + (long)nsm * waves - 1) / ((long)nsm * waves));
+      const int need = (nchains + wpc - 1) / wpc;
       plan->kind = K_WARP;
       plan->warps_per_cta = wpc;
       plan->grid = need < nsm ? need : nsm;
@@ -1569,18 +2086,33 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   }
   // one CTA of 16 warps per chain, label sets in HBM
   if (hint == 1) return cudaErrorNotSupported;
-  BlockSmem bs = BlockSmem::make(L, 1);
+  BlockSmem bs = BlockSmem::make(L, slice_moves);
   if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
   plan->kind = K_BLOCK;
   plan->warps_per_cta = 16;
   plan->grid = nchains;
   plan->smem = bs.total;
+  plan->cluster = 1;
+  // par order with chunk summaries and at most half as many chains as SMs: a pair of CTAs per chain,
+  // if every pair can be resident at once
+  const bool pair_ok = L.sums && order == 0 && slice_moves == 0;
+  if (hint == 4 && !pair_ok) return cudaErrorNotSupported;
+  if (pair_ok && (hint == 4 || (hint == 0 && 2 * nchains <= nsm))) {
+    const int grid = 2 * nchains;
+    if (cluster_capacity(bs.total, grid) >= (hint == 4 ? 1 : nchains)) {
+      plan->grid = grid;
+      plan->cluster = 2;
+    } else if (hint == 4) {
+      return cudaErrorNotSupported;
+    }
+  }
   return cudaSuccess;
 }
 
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
   if (p.kind == K_PAIR) return launch_pair(a, p, st);
   if (p.kind == K_WARP) return a.order == 0 ? launch_warp_o<0>(a, p, st) : launch_warp_o<1>(a, p, st);
+  if (p.cluster == 2) return launch_cluster(a, p, st);
   if (a.L.sums) return a.order == 0 ? launch_block_t<true, 0>(a, p, st) : launch_block_t<true, 1>(a, p, st);
   return a.order == 0 ? launch_block_t<false, 0>(a, p, st) : launch_block_t<false, 1>(a, p, st);
 }

@@ -56,10 +56,12 @@ struct LaunchPlan {
   int warps_per_cta;         // chains per CTA (K_WARP), warps per chain (K_BLOCK), chain pairs (K_PAIR)
   int grid;
   size_t smem;
+  int cluster = 1;           // K_BLOCK: CTAs per chain (2: k_anneal_cluster)
 };
 
 // Host-side entry points (tsa_kernels.cu).
-// hint: 0 auto, 1 one warp per chain, 2 one CTA per chain (label sets in HBM), 3 two warps per chain
+// hint: 0 auto, 1 one warp per chain, 2 one CTA per chain (label sets in HBM), 3 two warps per chain,
+// 4 a pair of CTAs per chain (par order with chunk summaries, no slice moves)
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
                         LaunchPlan* plan);
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
