@@ -915,14 +915,17 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
 // ================================================================================================
 // With chunk summaries, a par phase is processed as a flat list of (node, chunk) items spread evenly over
 // the CTA's threads (see par_phase_flat); these are its per-batch tables.
-constexpr int kFlatBatch = 512;   // nodes per batch (one owner thread each)
-constexpr int kFlatItems = 8192;  // (node, chunk) items per window
+constexpr int kFlatBatch = 512;            // nodes per batch (one owner thread each)
+constexpr int kFlatItems = 8192;           // (node, chunk) items per window
+constexpr uint32_t kLeafSumCache = 220u << 10;  // cache leaf summaries in shared memory below this total
 
 struct BlockSmem {
   uint32_t off_ch, off_cz, off_cz2, off_sum, off_S, off_pri, off_par, off_wl, off_U, off_U2, total;
-  uint32_t off_ninfo, off_nrnd, off_ncnt, off_nxs, off_nacc, off_items, off_scan;
+  uint32_t off_ninfo, off_nrnd, off_ncnt, off_nxs, off_nacc, off_noff, off_nu, off_scan, off_lsum, off_items;
   int nint2;
-  __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves) {
+  // pair: the layout of k_anneal_cluster, which also keeps the leaf chunk summaries in shared memory (its
+  // label loads bypass L1; the single-CTA kernel leaves that room to L1, which serves its reloads)
+  __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves, bool pair = false) {
     BlockSmem b;
     b.nint2 = (int)rnd_up((uint32_t)L.nint, 8);
     const uint32_t n2 = (uint32_t)b.nint2;
@@ -955,7 +958,11 @@ struct BlockSmem {
       o += 8 * kFlatBatch;
       b.off_nxs = o;
       o += 8 * kFlatBatch;
+      b.off_nu = o;
+      o += 8 * kFlatBatch;
       b.off_nrnd = o;
+      o += 4 * kFlatBatch;
+      b.off_noff = o;
       o += 4 * kFlatBatch;
       b.off_items = o;
       o += 4 * kFlatItems;
@@ -963,8 +970,16 @@ struct BlockSmem {
       o += 4 * 32;
       b.off_nacc = o;
       o += kFlatBatch;
+      // leaf chunk summaries, when they fit (otherwise read from global memory)
+      o = rnd_up(o, 16);
+      b.off_lsum = 0;
+      if (pair && o + 8u * (uint32_t)L.m <= kLeafSumCache) {
+        b.off_lsum = o;
+        o += 8u * (uint32_t)L.m;
+      }
     } else {
-      b.off_ninfo = b.off_ncnt = b.off_nxs = b.off_nrnd = b.off_items = b.off_scan = b.off_nacc = 0;
+      b.off_ninfo = b.off_ncnt = b.off_nxs = b.off_nrnd = b.off_noff = b.off_nu = b.off_scan = b.off_nacc = 0;
+      b.off_lsum = b.off_items = 0;
     }
     b.total = rnd_up(o, 128);
     return b;
@@ -1281,11 +1296,12 @@ __device__ __forceinline__ int pick_group(int k, int T) {
 //   1. one owner thread per node draws the rule (Philox), finds P, O, K, M and the chunk union u;
 //   2. a block-wide exclusive scan of popc(u) numbers the batch's chunk items;
 //   3. every thread takes items e = tid, tid + T, ... (two at a time, all eight 16-byte loads issued
-//      before any is used) and adds the item's popcounts (sx, |K&O&~X|, |X&M&~D|, packed into one u64)
-//      and the nonzero bit of X into the node's shared-memory totals;
+//      before any is used), finds each item's node by a binary search over the batch's item offsets
+//      and its chunk as the k-th set bit of u, and adds the item's popcounts (sx | k2 << 16, k3) and
+//      nonzero bit of X into the node's shared-memory totals with 32-bit atomics;
 //   4. the owner evaluates dE and the Metropolis test and rewrites the node's metadata on accept;
-//   5. the items of accepted nodes are recomputed (their sets are unchanged by the phase) and X is
-//      stored into P's chunks.
+//   5. X is stored into P's chunks for the items of accepted nodes (a thread's first two items from
+//      registers, any further ones recomputed: the sets they read are unchanged by the phase).
 // Same moves, same random numbers and the same integer counts as visit_coop, so the chains are
 // bit-identical; only the schedule of the loads changes.
 // ------------------------------------------------------------------------------------------------
@@ -1295,57 +1311,111 @@ struct FlatTabs {
   uint2* cnt;     // [batch] counts: x = sx | k2 << 16, y = k3 (each at most 64 * 128)
   uint2* xs;      // [batch] chunk summary of X: x = chunks 0-31, y = chunks 32-63
   uint8_t* acc;   // [batch] accepted
+  uint32_t* off;  // [batch] number of the node's first item
+  uint64_t* u;    // [batch] chunk union of the node's four sets
   uint32_t* items;  // [window] node << 16 | chunk
   int* scan;      // [32] per-warp totals
 };
 
-// Pass 0 returns the item's counts (sx | k2 << 16, k3) and its nonzero bit of X; pass 1 stores X.
-struct ItemCounts {
+struct Item {
+  int j, c;  // node of the batch, chunk
+};
+__device__ __forceinline__ Item item_of(uint32_t it) { return Item{(int)(it >> 16), (int)(it & 0xFFFFu)}; }
+
+// The items numbered [w0, w0 + kFlatItems) into F.items.  A warp whose owners have fewer than 32 chunks
+// each lets every owner write its own items (as many steps as the widest owner has chunks); otherwise
+// the warp expands the masks of its 32 owners together: for owner o, lane l writes the item of chunk l
+// (and 32 + l) if that bit is set, at the owner's offset plus the number of set bits below it.
+__device__ __forceinline__ void flat_build(const FlatTabs& F, int nb, int w0) {
+  const int tid = threadIdx.x, lane = tid & 31, wbase = tid & ~31;
+  const uint32_t lt = (1u << lane) - 1u;
+  const uint64_t myu = tid < nb ? F.u[tid] : 0ull;
+  int wide = __popcll(myu);
+  for (int o = 16; o > 0; o >>= 1) wide = max(wide, __shfl_xor_sync(0xFFFFFFFFu, wide, o));
+  if (wide < 32) {
+    uint64_t uu = myu;
+    for (int k = (int)(tid < nb ? F.off[tid] : 0) - w0; uu; k++) {
+      const int c = __ffsll((long long)uu) - 1;
+      uu &= uu - 1;
+      if (k >= 0 && k < kFlatItems) F.items[k] = ((uint32_t)tid << 16) | (uint32_t)c;
+    }
+    return;
+  }
+  for (int o = 0; o < 32; o++) {
+    const int j = wbase + o;
+    if (j >= nb) break;
+    const uint64_t u = F.u[j];
+    if (!u) continue;
+    const int base = (int)F.off[j] - w0;
+    const uint32_t lo = (uint32_t)u, hi = (uint32_t)(u >> 32);
+    const int klo = base + __popc(lo & lt), khi = base + __popc(lo) + __popc(hi & lt);
+    if (((lo >> lane) & 1u) && klo >= 0 && klo < kFlatItems) F.items[klo] = ((uint32_t)j << 16) | (uint32_t)lane;
+    if (((hi >> lane) & 1u) && khi >= 0 && khi < kFlatItems)
+      F.items[khi] = ((uint32_t)j << 16) | (uint32_t)(32 + lane);
+  }
+}
+
+// X of one item and its counts: a = sx | k2 << 16, b = k3, (xlo, xhi) = its bit of X's summary
+struct ItemX {
+  ulonglong2 x;
   uint32_t a, b, xlo, xhi;
 };
-template <int PASS, int CL>
-__device__ __forceinline__ ItemCounts flat_item(const BlkCtx& B, const FlatTabs& F, const uint16_t* wlb, uint32_t it) {
-  const int m = B.m, nw = B.nw;
-  const int j = (int)(it >> 16), c = (int)(it & 0xFFFFu);
-  if (PASS == 1 && !F.acc[j]) return ItemCounts{};
-  const uint2 inf = F.info[j];
-  const int Pn = (int)(inf.x & 0xFFFFu), On = (int)(inf.x >> 16), Kn = (int)(inf.y & 0xFFFFu),
-            Mn = (int)(inf.y >> 16);
-  const int q = wlb[j];
+// the item's chunk of D, O, K and M
+struct ItemSets {
+  ulonglong2 d, o, k, m;
+};
+template <int CL>
+__device__ __forceinline__ ItemSets flat_load(const BlkCtx& B, const FlatTabs& F, const uint16_t* wlb, Item it) {
+  const int m = B.m, nw = B.nw, c = it.c;
+  const uint2 inf = F.info[it.j];
+  const int On = (int)(inf.x >> 16), Kn = (int)(inf.y & 0xFFFFu), Mn = (int)(inf.y >> 16);
+  const int q = wlb[it.j];
   auto ptr = [&](int n) { return n >= m ? B.lab + (size_t)(n - m) * nw : B.leaf + (size_t)n * nw; };
-  const uint64_t* gD = B.lab + (size_t)q * nw + 2 * c;
   auto L2 = [](const uint64_t* p) { return CL == 1 ? ld2(p) : ld2_cg(p); };
-  const ulonglong2 d = L2(gD), o = L2(ptr(On) + 2 * c), k = L2(ptr(Kn) + 2 * c), mm = L2(ptr(Mn) + 2 * c);
-  const uint64_t x0 = (k.x | o.x) & (mm.x | d.x), x1 = (k.y | o.y) & (mm.y | d.y);
-  if (PASS == 1) {
-    *reinterpret_cast<ulonglong2*>(B.lab + (size_t)(Pn - m) * nw + 2 * c) = make_ulonglong2(x0, x1);
-    return ItemCounts{};
-  }
+  ItemSets v;
+  v.d = L2(B.lab + (size_t)q * nw + 2 * c);
+  v.o = L2(ptr(On) + 2 * c);
+  v.k = L2(ptr(Kn) + 2 * c);
+  v.m = L2(ptr(Mn) + 2 * c);
+  return v;
+}
+__device__ __forceinline__ ItemX flat_compute(const BlkCtx& B, Item it, const ItemSets& v) {
+  const int c = it.c;
+  const ulonglong2 d = v.d, o = v.o, k = v.k, mm = v.m;
+  ItemX r;
+  r.x = make_ulonglong2((k.x | o.x) & (mm.x | d.x), (k.y | o.y) & (mm.y | d.y));
   uint64_t n0 = ~0ull, n1 = ~0ull;
   if (B.slicing) {
     n0 = ~B.S[2 * c];
     n1 = ~B.S[2 * c + 1];
   }
-  const uint64_t xm0 = x0 & n0, xm1 = x1 & n1;
+  const uint64_t xm0 = r.x.x & n0, xm1 = r.x.y & n1;
   const uint32_t sx = (uint32_t)(__popcll(xm0) + __popcll(xm1));
-  const uint32_t k2 = (uint32_t)(__popcll(k.x & o.x & ~x0 & n0) + __popcll(k.y & o.y & ~x1 & n1));
-  const uint32_t k3 = (uint32_t)(__popcll(xm0 & mm.x & ~d.x) + __popcll(xm1 & mm.y & ~d.y));
-  const uint32_t nz = (x0 | x1) ? 1u : 0u;
-  return ItemCounts{sx | (k2 << 16), k3, c < 32 ? nz << c : 0u, c >= 32 ? nz << (c - 32) : 0u};
+  const uint32_t k2 = (uint32_t)(__popcll(k.x & o.x & ~r.x.x & n0) + __popcll(k.y & o.y & ~r.x.y & n1));
+  r.a = sx | (k2 << 16);
+  r.b = (uint32_t)(__popcll(xm0 & mm.x & ~d.x) + __popcll(xm1 & mm.y & ~d.y));
+  const uint32_t nz = (r.x.x | r.x.y) ? 1u : 0u;
+  r.xlo = c < 32 ? nz << c : 0u;
+  r.xhi = c >= 32 ? nz << (c - 32) : 0u;
+  return r;
+}
+template <int CL>
+__device__ __forceinline__ ItemX flat_eval(const BlkCtx& B, const FlatTabs& F, const uint16_t* wlb, Item it) {
+  return flat_compute(B, it, flat_load<CL>(B, F, wlb, it));
 }
 
-// Add one item per lane into its node's totals: the lanes of a node (adjacent items) are found with
-// match.any and reduced with redux.sync, so each node takes one shared-memory atomic per warp.
-__device__ __forceinline__ void flat_add(const FlatTabs& F, int j, const ItemCounts& v) {
-  const unsigned peers = __match_any_sync(0xFFFFFFFFu, j);
-  const uint32_t a = __reduce_add_sync(peers, v.a), b = __reduce_add_sync(peers, v.b);
-  const uint32_t xlo = __reduce_or_sync(peers, v.xlo), xhi = __reduce_or_sync(peers, v.xhi);
-  if (j >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1) {
-    atomicAdd(&F.cnt[j].x, a);
-    atomicAdd(&F.cnt[j].y, b);
-    if (xlo) atomicOr(&F.xs[j].x, xlo);
-    if (xhi) atomicOr(&F.xs[j].y, xhi);
-  }
+// Add one item into its node's totals: 32-bit shared-memory atomics (lanes of one node serialise only
+// among themselves; a warp-level match/reduce first measured several times slower).
+__device__ __forceinline__ void flat_add(const FlatTabs& F, int j, const ItemX& v) {
+  atomicAdd(&F.cnt[j].x, v.a);
+  if (v.b) atomicAdd(&F.cnt[j].y, v.b);
+  if (v.xlo) atomicOr(&F.xs[j].x, v.xlo);
+  if (v.xhi) atomicOr(&F.xs[j].y, v.xhi);
+}
+
+__device__ __forceinline__ void flat_store(const BlkCtx& B, const FlatTabs& F, Item it, ulonglong2 x) {
+  const int Pn = (int)(F.info[it.j].x & 0xFFFFu);
+  *reinterpret_cast<ulonglong2*>(B.lab + (size_t)(Pn - B.m) * B.nw + 2 * it.c) = x;
 }
 
 // CL = 2: one CTA of a pair; metadata writes go to both CTAs' copies (P: the other CTA's arrays).
@@ -1361,7 +1431,6 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     // 1. owners: rule, pivot and chunk union
     int q = 0, nck = 0;
     bool prop = false;
-    uint64_t u = 0;
     uint32_t chv = 0;
     if (tid < nb) {
       q = wlb[tid];
@@ -1370,6 +1439,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       const bool li = l >= m, ri = r >= m;
       prop = li || ri;
       uint2 inf = make_uint2(0xFFFFFFFFu, 0xFFFFFFFFu);
+      uint64_t u = 0;
       if (prop) {
         const U4 rnd = philox10((uint32_t)(m + q), sweep, chain, 0u, B.key0, B.key1);
         const int rule = pick_rule(li, ri, rnd.x);
@@ -1385,6 +1455,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
         F.rnd[tid] = rnd.y;
       }
       F.info[tid] = inf;
+      F.u[tid] = u;
       F.cnt[tid] = make_uint2(0u, 0u);
       F.xs[tid] = make_uint2(0u, 0u);
     }
@@ -1405,34 +1476,42 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       F.scan[lane] = v;
     }
     __syncthreads();
-    const int off = incl - nck + (warp ? F.scan[warp - 1] : 0);
+    if (tid < nb) F.off[tid] = (uint32_t)(incl - nck + (warp ? F.scan[warp - 1] : 0));
     const int total = F.scan[nwarps - 1];
-    auto build = [&](int w0) {  // the items numbered [w0, w0 + kFlatItems)
-      if (nck && off < w0 + kFlatItems && off + nck > w0) {
-        uint64_t uu = u;
-        for (int k = off; uu; k++) {
-          const int c = __ffsll((long long)uu) - 1;
-          uu &= uu - 1;
-          if (k >= w0 && k < w0 + kFlatItems) F.items[k - w0] = ((uint32_t)tid << 16) | (uint32_t)c;
-        }
-      }
-    };
-    // 3. counts of every item
+    __syncthreads();
+    // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first two items
+    Item k0{-1, 0}, k1{-1, 0};
+    ulonglong2 x0 = make_ulonglong2(0ull, 0ull), x1 = x0;
     for (int w0 = 0; w0 < total; w0 += kFlatItems) {
       if (w0) __syncthreads();  // the previous window's items are consumed
-      build(w0);
+      flat_build(F, nb, w0);
       __syncthreads();
       const int nwin = min(kFlatItems, total - w0);
-      // warp-uniform trip count: every lane takes part in the reductions
-      for (int e0 = warp * 32; e0 < nwin; e0 += 2 * T) {
-        const int e = e0 + lane, e1 = e + T;
-        const bool v0 = e < nwin, v1 = e1 < nwin;
-        const uint32_t i0 = v0 ? F.items[e] : 0u, i1 = v1 ? F.items[e1] : 0u;
-        const ItemCounts c0 = v0 ? flat_item<0, CL>(B, F, wlb, i0) : ItemCounts{};
-        const ItemCounts c1 = v1 ? flat_item<0, CL>(B, F, wlb, i1) : ItemCounts{};
-        flat_add(F, v0 ? (int)(i0 >> 16) : -1, c0);
-        if (e0 + T < nwin) flat_add(F, v1 ? (int)(i1 >> 16) : -1, c1);
-        cnt.busy += (unsigned long long)(v0 + v1);
+      int e = tid;
+      for (; e + T < nwin; e += 2 * T) {  // two items: all eight loads issued before either is used
+        const Item i0 = item_of(F.items[e]), i1 = item_of(F.items[e + T]);
+        const ItemSets s0 = flat_load<CL>(B, F, wlb, i0);
+        const ItemSets s1 = flat_load<CL>(B, F, wlb, i1);
+        const ItemX r0 = flat_compute(B, i0, s0), r1 = flat_compute(B, i1, s1);
+        flat_add(F, i0.j, r0);
+        flat_add(F, i1.j, r1);
+        if (w0 == 0 && e == tid) {
+          k0 = i0;
+          x0 = r0.x;
+          k1 = i1;
+          x1 = r1.x;
+        }
+        cnt.busy += 2;
+      }
+      if (e < nwin) {
+        const Item i0 = item_of(F.items[e]);
+        const ItemX r0 = flat_eval<CL>(B, F, wlb, i0);
+        flat_add(F, i0.j, r0);
+        if (w0 == 0 && e == tid) {
+          k0 = i0;
+          x0 = r0.x;
+        }
+        cnt.busy++;
       }
     }
     __syncthreads();
@@ -1475,21 +1554,23 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       cnt.visits++;
     }
     __syncthreads();
-    // 5. X into the pivots of accepted moves
+    // 5. X into the pivots of accepted moves: the two kept items from registers, the rest recomputed
+    if (k0.j >= 0 && F.acc[k0.j]) flat_store(B, F, k0, x0);
+    if (k1.j >= 0 && F.acc[k1.j]) flat_store(B, F, k1, x1);
+    const bool rebuild = total > kFlatItems;  // the list in shared memory is the last window's
     for (int w0 = 0; w0 < total; w0 += kFlatItems) {
-      if (total > kFlatItems) {
-        __syncthreads();
-        build(w0);
-        __syncthreads();
-      }
+      const int first = w0 == 0 ? 2 * T : 0;  // window 0's items [0, 2T) were kept in registers
       const int nwin = min(kFlatItems, total - w0);
-      int e = tid;
-      for (; e + T < nwin; e += 2 * T) {
-        const uint32_t i0 = F.items[e], i1 = F.items[e + T];
-        flat_item<1, CL>(B, F, wlb, i0);
-        flat_item<1, CL>(B, F, wlb, i1);
+      if (nwin <= first) continue;  // uniform
+      if (rebuild) {
+        __syncthreads();
+        flat_build(F, nb, w0);
+        __syncthreads();
       }
-      if (e < nwin) flat_item<1, CL>(B, F, wlb, F.items[e]);
+      for (int e = first + tid; e < nwin; e += T) {
+        const Item it = item_of(F.items[e]);
+        if (F.acc[it.j]) flat_store(B, F, it, flat_eval<CL>(B, F, wlb, it).x);
+      }
     }
     __syncthreads();
   }
@@ -1543,8 +1624,15 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   F.cnt = reinterpret_cast<uint2*>(smem + Bm.off_ncnt);
   F.xs = reinterpret_cast<uint2*>(smem + Bm.off_nxs);
   F.acc = smem + Bm.off_nacc;
+  F.off = reinterpret_cast<uint32_t*>(smem + Bm.off_noff);
+  F.u = reinterpret_cast<uint64_t*>(smem + Bm.off_nu);
   F.items = reinterpret_cast<uint32_t*>(smem + Bm.off_items);
   F.scan = reinterpret_cast<int*>(smem + Bm.off_scan);
+  if (Bm.off_lsum) {  // leaf chunk summaries cached in shared memory
+    uint64_t* ls = reinterpret_cast<uint64_t*>(smem + Bm.off_lsum);
+    for (int q = tid; q < L.m; q += T) ls[q] = a.leaf_sum[q];
+    B.leaf_sum = ls;
+  }
   Counters cnt{};
   __syncthreads();
   for (int c = blockIdx.x; c < a.nchains; c += gridDim.x) {
@@ -1752,7 +1840,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
   cg::cluster_group cl = cg::this_cluster();
   const int rank = (int)cl.block_rank();
   const Layout L = a.L;
-  const BlockSmem Bm = BlockSmem::make(L, a.slice_moves);
+  const BlockSmem Bm = BlockSmem::make(L, a.slice_moves, true);
   const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31;
   const unsigned FULL = 0xFFFFFFFFu;
   float* s_lse = reinterpret_cast<float*>(smem);
@@ -1796,8 +1884,15 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
   F.cnt = reinterpret_cast<uint2*>(smem + Bm.off_ncnt);
   F.xs = reinterpret_cast<uint2*>(smem + Bm.off_nxs);
   F.acc = smem + Bm.off_nacc;
+  F.off = reinterpret_cast<uint32_t*>(smem + Bm.off_noff);
+  F.u = reinterpret_cast<uint64_t*>(smem + Bm.off_nu);
   F.items = reinterpret_cast<uint32_t*>(smem + Bm.off_items);
   F.scan = reinterpret_cast<int*>(smem + Bm.off_scan);
+  if (Bm.off_lsum) {  // leaf chunk summaries cached in shared memory
+    uint64_t* ls = reinterpret_cast<uint64_t*>(smem + Bm.off_lsum);
+    for (int q = tid; q < L.m; q += T) ls[q] = a.leaf_sum[q];
+    B.leaf_sum = ls;
+  }
   PeerArrays P;
   P.ch = cl.map_shared_rank(B.ch, rank ^ 1);
   P.cz = cl.map_shared_rank(B.cz, rank ^ 1);
@@ -2017,7 +2112,7 @@ static cudaLaunchConfig_t cluster_config(int grid, size_t smem, cudaStream_t st,
 }
 
 static cudaError_t launch_cluster(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
-  size_t smem = BlockSmem::make(a.L, a.slice_moves).total;
+  size_t smem = BlockSmem::make(a.L, a.slice_moves, true).total;
   cudaError_t e = cudaFuncSetAttribute(k_anneal_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute attr[1];
@@ -2099,9 +2194,11 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   if (hint == 4 && !pair_ok) return cudaErrorNotSupported;
   if (pair_ok && (hint == 4 || (hint == 0 && 2 * nchains <= nsm))) {
     const int grid = 2 * nchains;
-    if (cluster_capacity(bs.total, grid) >= (hint == 4 ? 1 : nchains)) {
+    const uint32_t psmem = BlockSmem::make(L, slice_moves, true).total;
+    if (psmem <= (uint32_t)optin && cluster_capacity(psmem, grid) >= (hint == 4 ? 1 : nchains)) {
       plan->grid = grid;
       plan->cluster = 2;
+      plan->smem = psmem;
     } else if (hint == 4) {
       return cudaErrorNotSupported;
     }
