@@ -2179,7 +2179,8 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
       return cudaSuccess;
     }
   }
-  // one CTA of 16 warps per chain, label sets in HBM
+  // one CTA of 16 warps per chain, label sets in HBM (smaller CTAs that fit several per SM measured
+  // slower: a chain's phases need the threads more than the SM needs more resident chains)
   if (hint == 1) return cudaErrorNotSupported;
   BlockSmem bs = BlockSmem::make(L, slice_moves);
   if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
