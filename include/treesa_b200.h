@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define TSA_ABI_VERSION 1
+#define TSA_ABI_VERSION 2
 
 enum {
   TSA_OK = 0,
@@ -89,7 +89,11 @@ typedef struct tsa_options {
                                  (label sets in HBM); 3 two warps per chain (par order); 4 a cluster of two
                                  CTAs per chain (par order, chunk summaries, no slice moves).  Never changes
                                  a result. */
-  int32_t reserved[12];
+  int32_t par_follow;         /* --par-follow (csrc/treesa_gpu.cu:1388): par order, an accepted first visit
+                                 re-visits its pivot child later in the sweep if the sweep already visited it */
+  int32_t par_band;           /* --par-band L (:1389): 0 off, or 2..16: par-order priorities top-down within
+                                 bands of L levels of the depth at the start of each sweep */
+  int32_t reserved[10];
 } tsa_options;
 
 /* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the

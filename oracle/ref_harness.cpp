@@ -37,11 +37,12 @@ extern "C" {
 // Chains c0..c0+nch-1 from trees_in / labels_in ([nch][m-1] words, [nch][m-1][nw64] u64 bitsets of
 // the internal nodes' output labels) and slice sets S_in ([nch][nw64] or NULL), nbetas levels of
 // niters sweeps each; order 0 = par, 1 = preorder.  Writes trees_out / labels_out (labels_out may be
-// NULL); counters = {proposals, accepts}; returns the seconds spent in the sweep loops.
+// NULL); counters = {proposals, accepts}; par_band / par_follow as the CLI's --par-band / --par-follow
+// (treesa_gpu.cu:1388-1389, 1524-1527); returns the seconds spent in the sweep loops.
 double ref_sweeps(int m, int nlab, const int* ix_off, const int* ix_lab, int order, uint64_t seed, double sc_target,
                   double sc_weight, const float* betas, int nbetas, int niters, int nch, int c0,
                   const uint32_t* trees_in, const uint64_t* labels_in, const uint64_t* S_in, uint32_t* trees_out,
-                  uint64_t* labels_out, long long* counters, int nthreads) {
+                  uint64_t* labels_out, long long* counters, int nthreads, int par_band, int par_follow) {
   fill_table();
   const int nw = (nlab + 63) / 64 > 0 ? (nlab + 63) / 64 : 1, nint = m - 1;
   Params P{};
@@ -49,6 +50,8 @@ double ref_sweeps(int m, int nlab, const int* ix_off, const int* ix_lab, int ord
   P.nint = nint;
   P.sc_target = (float)sc_target;
   P.sc_weight = (float)sc_weight;
+  P.par_band = par_band;
+  P.par_follow = par_follow;
   uint64_t k = splitmix64_h(seed);
   P.key0 = (uint32_t)k;
   P.key1 = (uint32_t)(k >> 32);

@@ -67,6 +67,14 @@ uint32_t par_pri(uint32_t v, uint32_t s, uint32_t c, uint32_t key0) {  // common
   uint32_t h = mix32(v * 0x9E3779B1u + mix32(s * 0x85EBCA77u + mix32(c ^ key0)));
   return (h >> 16) | 1u;
 }
+// par_band L: band position of the depth d at the start of the sweep, then the node's own bits (common.h:264-268)
+uint32_t par_band_pri(uint32_t v, uint32_t s, uint32_t c, uint32_t key0, int d, int L) {
+  return ((uint32_t)((L - 1 - d % L) & 15) << 12) | (par_pri(v, s, c, key0) & 0x0FFEu) | 1u;
+}
+// par_follow: even priority of a follow-up visit; hs = mix32(s * 0x85EBCA77 + mix32(c ^ key0)) (common.h:269-272)
+uint32_t par_follow_pri(uint32_t v, uint32_t hs) {
+  return ((mix32((v * 0x9E3779B1u + hs) ^ 0x5BD1E995u) >> 16) & 0xFFFEu) | 2u;
+}
 
 int pick_rule(bool li, bool ri, uint32_t r) {  // common.h:233-238
   if (li && ri) return (int)(r >> 30);
@@ -248,6 +256,7 @@ struct Par {
   int m, nint, nw, leaf_sc, slicing, slice_moves, slice_every, max_slices;
   float sc_target, sc_weight;
   uint32_t key0, key1;
+  int par_band, par_follow;  // par-order variants (off: 0)
 };
 
 inline const uint64_t* set_of(const Inst& I, const Chain& C, int v) {
@@ -341,7 +350,10 @@ void preorder_sweep(const Inst& I, const Par& P, Chain& C, float beta, uint32_t 
   }
 }
 
-// par sweep: cpu_ref.h:133-182 (no par_band / par_follow)
+// par sweep: cpu_ref.h:133-182.  par_band: priorities from the depth at the start of the sweep
+// (cpu_ref.h:140-151); par_follow: an accepted first visit re-arms its pivot child if the sweep already
+// visited it, and a follow-up visit (even priority) draws Philox with the sweep's top bit set
+// (cpu_ref.h:168-175).
 void par_sweep(const Inst& I, const Par& P, Chain& C, float beta, uint32_t sweep, uint32_t chain, long long& np,
                long long& na, long long* nphase) {
   const int m = I.m, n = 2 * m - 1;
@@ -352,6 +364,20 @@ void par_sweep(const Inst& I, const Par& P, Chain& C, float beta, uint32_t sweep
   }
   std::vector<uint32_t> pri(n, 0);
   for (int v = m; v < n; v++) pri[v] = par_pri((uint32_t)v, sweep, chain, P.key0);
+  if (P.par_band > 0) {
+    std::vector<int> dep(n, 0), st{n - 1};
+    while (!st.empty()) {
+      int v = st.back();
+      st.pop_back();
+      if (v < m) continue;
+      int l = (int)(C.ch[v - m] & 0xFFFFu), r = (int)(C.ch[v - m] >> 16);
+      dep[l] = dep[r] = dep[v] + 1;
+      st.push_back(l);
+      st.push_back(r);
+    }
+    for (int v = m; v < n; v++) pri[v] = par_band_pri((uint32_t)v, sweep, chain, P.key0, dep[v], P.par_band);
+  }
+  const uint32_t hs = mix32(sweep * 0x85EBCA77u + mix32(chain ^ P.key0));
   auto key = [&](int u) { return (pri[u] << 16) | (uint32_t)u; };
   std::vector<int> act;
   for (;;) {
@@ -369,7 +395,14 @@ void par_sweep(const Inst& I, const Par& P, Chain& C, float beta, uint32_t sweep
     if (act.empty()) break;
     if (nphase) (*nphase)++;
     for (int v : act) {
-      visit(I, P, C, v, beta, sweep, chain, np, na);
+      const bool rev = (pri[v] & 1u) == 0;
+      const uint32_t before = C.ch[v - m];
+      visit(I, P, C, v, beta, rev ? (sweep | 0x80000000u) : sweep, chain, np, na);
+      if (P.par_follow && !rev && C.ch[v - m] != before) {
+        const int l0 = (int)(before & 0xFFFFu), r0 = (int)(before >> 16);
+        const int Pn = (int)(C.ch[v - m] & 0xFFFFu) == l0 ? l0 : r0;  // the pivot keeps its slot
+        if (!pri[Pn]) pri[Pn] = par_follow_pri((uint32_t)Pn, hs);
+      }
       int l = (int)(C.ch[v - m] & 0xFFFFu), r = (int)(C.ch[v - m] >> 16);
       parent[l] = v;
       parent[r] = v;
@@ -647,6 +680,8 @@ Par make_par(const Inst& I, const tsa_options* O) {  // Runner ctor, treesa_gpu.
   P.max_slices = O->max_slices > 0 ? O->max_slices : I.nlab;
   P.sc_target = (float)O->sc_target;
   P.sc_weight = (float)O->sc_weight;
+  P.par_band = O->par_band;
+  P.par_follow = O->par_follow ? 1 : 0;
   uint64_t k = splitmix64(O->seed);
   P.key0 = (uint32_t)k;
   P.key1 = (uint32_t)(k >> 32);
@@ -892,13 +927,15 @@ void orc_result_free(tsa_result* r) {
 // start from trees_in (and slice sets S_in, [nch][nw] u64, or NULL) and run nbetas levels of niters
 // sweeps with sweep id lev*niters+it; fixed slice sets (no slice moves).  Writes the final trees and
 // labels.  counters: [0] proposals, [1] accepts, [2] phases.
-int orc_sweeps(const tsa_instance* inst, int order, uint64_t seed, double sc_target, double sc_weight,
-               const float* betas, int nbetas, int niters, int nch, int c0, const uint32_t* trees_in,
-               const uint64_t* S_in, uint32_t* trees_out, uint64_t* labels_out, long long* counters, char* err,
-               size_t errlen) {
+int orc_sweeps(const tsa_instance* inst, int order, int par_band, int par_follow, uint64_t seed, double sc_target,
+               double sc_weight, const float* betas, int nbetas, int niters, int nch, int c0,
+               const uint32_t* trees_in, const uint64_t* S_in, uint32_t* trees_out, uint64_t* labels_out,
+               long long* counters, char* err, size_t errlen) {
   Inst I;
   if (!load_instance(inst, I, err, errlen)) return TSA_ERR_ARG;
   tsa_options O{};
+  O.par_band = par_band;
+  O.par_follow = par_follow;
   O.sc_target = sc_target;
   O.sc_weight = sc_weight;
   O.seed = seed;

@@ -15,7 +15,9 @@ Writes
                      schedule (48 chains, betas 0.2:0.7:7, 4 sweeps, sc_target 24, seed 7), chains
                      0..3 from the greedy tree, 4..7 random;
                      (c) the sq32/sq48 row-major-start results of the reference's large-network
-                     benchmark log (bench/results/large_compare_gpu_par.jsonl), par order.
+                     benchmark log (bench/results/large_compare_gpu_par.jsonl), par order;
+                     (d) as (b) in par order with the CLI's --par-band L and --par-follow variants
+                     (csrc/cpu_ref.h:140-175).
 """
 import hashlib
 import json
@@ -105,6 +107,19 @@ def main(ref):
             cpuref.append(dict(instance=name, order=order, betas=[0.2, 0.7, 7.0], niters=4, seed=7, sc_target=24.0,
                                nchains=8, proposals=int(cnt[0]), accepts=int(cnt[1]), sha256=digest(t, l)))
 
+    # (d) par-order variants: band priorities and follow-up visits
+    variants = []
+    for name in ("sat60", "reg3_250", "lat14", "grid24"):
+        rec = inst[name]
+        net = O.Net(rec["ixs"], rec["iy"], rec["nlab"])
+        trees = np.stack([tree_words(rec["tree"])] * 4 + [O.random_tree(net.m, 7, c) for c in range(4, 8)])
+        for band, follow in ((0, 1), (2, 0), (5, 1), (16, 0)):
+            t, l, cnt, _ = O.ref_sweeps(net, trees, betas, 4, order="par", seed=7, sc_target=24.0, par_band=band,
+                                        par_follow=bool(follow))
+            variants.append(dict(instance=name, order="par", par_band=band, par_follow=follow, betas=[0.2, 0.7, 7.0],
+                                 niters=4, seed=7, sc_target=24.0, nchains=8, proposals=int(cnt[0]),
+                                 accepts=int(cnt[1]), sha256=digest(t, l)))
+
     # (c) sq32 / sq48 from the row-major path tree (tc / sc identical on RTX 6000 and H100)
     large = []
     for line in open(os.path.join(ref, "bench", "results", "large_compare_gpu_par.jsonl")):
@@ -113,8 +128,9 @@ def main(ref):
             large.append(dict(instance=r["instance"], nchains=r["nchains"], niters=r["niters"], beta0=r["beta0"],
                               tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
     with open(os.path.join(HERE, "expected.json"), "w") as f:
-        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large), f, indent=1)
-    print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}")
+        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants), f, indent=1)
+    print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}, "
+          f"variants {len(variants)}")
 
 
 if __name__ == "__main__":

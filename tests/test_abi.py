@@ -55,6 +55,10 @@ def test_argument_errors_are_reported_not_fatal():
     rc, msg = _create(tri, init_slices=[7])
     assert rc == 1 and "init_slices" in msg
     assert _create(tri, rank=2, world_size=2)[0] == 1
+    rc, msg = _create(tri, par_band=1)  # the reference's --par-band check (csrc/treesa_gpu.cu:1527)
+    assert rc == 1 and "2..16" in msg
+    assert _create(tri, par_band=17)[0] == 1
+    assert _create(tri, kernel_hint=3, par_follow=True)[0] == 1
 
 
 def test_run_reports_errors_through_the_python_api():

@@ -28,9 +28,10 @@ def _net(rec):
     return engine.Network(rec["ixs"], rec["iy"], rec["nlab"]), O.Net(rec["ixs"], rec["iy"], rec["nlab"])
 
 
-def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None, kernel="auto"):
+def _gpu_sweeps(net, trees, betas, niters, order, seed, sc_target, S=None, kernel="auto", par_band=0,
+                par_follow=False):
     opts = dict(betas=betas, niters=niters, nchains=len(trees), sc_target=sc_target, order=order, seed=seed,
-                init_trees=trees, kernel_hint=kernel)
+                init_trees=trees, kernel_hint=kernel, par_band=par_band, par_follow=par_follow)
     if S is not None:
         opts["init_slices"] = S
     s = engine.Session(net, **opts)
@@ -67,6 +68,39 @@ def test_trajectories_bit_exact(name, order, kernel):
     assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
     if order == "par":
         assert st["phases"] == ocnt[2]
+
+
+@pytest.mark.parametrize("kernel", ["warp", "block"])
+def test_par_variants_match_reference_digests(kernel, golden):
+    """--par-band L and --par-follow (csrc/cpu_ref.h:140-175): the digests of the reference's own output."""
+    for e in golden[1]["variants"]:
+        if e["instance"] in WIDE and kernel != "block":
+            continue
+        rec = _util.instance(e["instance"])
+        net, onet = _net(rec)
+        trees = _util.start_trees(rec, 8, seed=7)
+        t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 4, "par", 7, 24.0, kernel=kernel, par_band=e["par_band"],
+                                 par_follow=bool(e["par_follow"]))
+        assert _util.digest(t, np.ascontiguousarray(lab[:, :, :onet.nw])) == e["sha256"], e
+        assert st["proposals"] == e["proposals"] and st["accepts"] == e["accepts"], e
+
+
+@pytest.mark.parametrize("kernel,band,follow", [("block", 4, True), ("block", 0, True), ("block", 11, False),
+                                                ("cta_pair", 6, False), ("warp", 3, True)])
+def test_par_variants_match_oracle(kernel, band, follow):
+    """The variants on the chunk-summary kernels (sq46) and on 64 chains of reg3_250, against the oracle."""
+    name = "reg3_250" if kernel == "warp" else "sq46"
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    nch = 64 if kernel == "warp" else 16
+    trees = _util.start_trees(rec, nch, seed=9)
+    t, lab, st = _gpu_sweeps(net, trees, CHECK_BETAS, 3, "par", 9, 22.0, kernel=kernel, par_band=band,
+                             par_follow=follow)
+    ot, olab, ocnt = O.sweeps(onet, trees, CHECK_BETAS, 3, order="par", seed=9, sc_target=22.0, par_band=band,
+                              par_follow=follow)
+    assert (t == ot).all(), f"{(t != ot).any(1).sum()} chains differ"
+    assert (lab[:, :, :onet.nw] == olab).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1] and st["phases"] == ocnt[2]
 
 
 @pytest.mark.parametrize("order", ["par", "preorder"])

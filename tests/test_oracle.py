@@ -56,6 +56,29 @@ def test_oracle_matches_cpu_ref_live(name, order):
     assert a[2][0] == b[2][0] and a[2][1] == b[2][1]
 
 
+def test_oracle_matches_cpu_ref_par_variants(golden):
+    """--par-band L and --par-follow (cpu_ref.h:140-175): the reference's own digests."""
+    for e in golden[1]["variants"]:
+        rec, net = _onet(e["instance"])
+        trees = _util.start_trees(rec, 8, seed=7)
+        t, lab, cnt = O.sweeps(net, trees, CHECK_BETAS, 4, order="par", seed=7, sc_target=24.0,
+                               par_band=e["par_band"], par_follow=bool(e["par_follow"]))
+        assert _util.digest(t, lab) == e["sha256"], e
+        assert cnt[0] == e["proposals"] and cnt[1] == e["accepts"], e
+
+
+@pytest.mark.skipif(not os.path.exists(O.CPUREF_SO), reason="reference harness not built (no reference sources)")
+@pytest.mark.parametrize("band,follow", [(3, True), (8, False), (0, True)])
+def test_oracle_matches_cpu_ref_live_variants(band, follow):
+    rec, net = _onet("reg3_100")
+    trees = _util.start_trees(rec, 16, seed=3)
+    betas = np.array([0.5 + 1.1 * i for i in range(6)], np.float32)
+    a = O.sweeps(net, trees, betas, 3, order="par", seed=3, sc_target=16.0, par_band=band, par_follow=follow)
+    b = O.ref_sweeps(net, trees, betas, 3, order="par", seed=3, sc_target=16.0, par_band=band, par_follow=follow)
+    assert (a[0] == b[0]).all() and (a[1] == b[1]).all()
+    assert a[2][0] == b[2][0] and a[2][1] == b[2][1]
+
+
 # PA rows whose float-energy selections the host libm does not reproduce (pinned on the GPU instead)
 PA_HOST_EXCEPTIONS = {("lat10", "par", "greedy"), ("lat10", "preorder", "random")}
 

@@ -10,7 +10,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtreesa_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 MODE = {"tc": 0, "gpu": 1, "h100": 2}
 SCHEME = {"indep": 0, "pa": 1, "trunc": 2}
@@ -38,7 +38,8 @@ class Options(C.Structure):
                 ("gpu_model", C.POINTER(C.c_double)), ("h100_model", C.POINTER(C.c_double)),
                 ("device", C.c_int32), ("stream", C.c_void_p), ("rank", C.c_int32), ("world_size", C.c_int32),
                 ("nccl_id", C.c_void_p), ("verbose", C.c_int32), ("max_levels", C.c_int32),
-                ("exp_mode", C.c_int32), ("kernel_hint", C.c_int32), ("reserved", C.c_int32 * 12)]
+                ("exp_mode", C.c_int32), ("kernel_hint", C.c_int32), ("par_follow", C.c_int32),
+                ("par_band", C.c_int32), ("reserved", C.c_int32 * 10)]
 
 
 class Result(C.Structure):
@@ -98,7 +99,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
                  order="par", seed=1, eval_every=1, slicing=False, slice_moves=1, slice_every=1, max_slices=0,
                  init_slices=(), select_sc=False, init_trees=None, gpu_model=None, h100_model=None, device=0,
                  stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc",
-                 exp_mode="host", kernel_hint=0):
+                 exp_mode="host", kernel_hint=0, par_follow=False, par_band=0):
     o = Options()
     o.betas, _ = keep.arr(np.asarray(betas, np.float32), np.float32, C.c_float)
     o.nbetas = len(betas)
@@ -141,6 +142,8 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
     o.exp_mode = {"host": 0, "device": 1}[exp_mode]
     o.kernel_hint = {0: 0, 1: 1, 2: 2, 3: 3, 4: 4, "auto": 0, "warp": 1, "block": 2, "pair": 3,
                      "cta_pair": 4}[kernel_hint]
+    o.par_follow = int(bool(par_follow))
+    o.par_band = int(par_band)
     return o
 
 

@@ -109,6 +109,18 @@ TSA_HD uint32_t mix32(uint32_t h) {
 TSA_HD uint32_t chain_hash(uint32_t chain, uint32_t key0) { return mix32(chain ^ key0); }
 TSA_HD uint32_t sweep_hash(uint32_t sweep, uint32_t hc) { return mix32(sweep * 0x85EBCA77u + hc); }
 TSA_HD uint32_t node_pri(uint32_t v, uint32_t hs) { return (mix32(v * 0x9E3779B1u + hs) >> 16) | 1u; }
+// par_band L (2..16): the band position of the node's depth d at the start of the sweep in the top four
+// bits (the top of each band of L levels first), the node's own priority bits below; odd, never 0
+// (csrc/common.h:264-268)
+TSA_HD uint32_t band_pri(uint32_t pri, int d, int L) {
+  return ((uint32_t)((L - 1 - d % L) & 15) << 12) | (pri & 0x0FFEu) | 1u;
+}
+// par_follow: priority of a follow-up visit of node v, even and nonzero (csrc/common.h:269-272)
+TSA_HD uint32_t follow_pri(uint32_t v, uint32_t hs) {
+  return ((mix32((v * 0x9E3779B1u + hs) ^ 0x5BD1E995u) >> 16) & 0xFFFEu) | 2u;
+}
+// a follow-up visit draws its own Philox stream: the sweep counter with its top bit set
+TSA_HD uint32_t follow_sweep(uint32_t sweep) { return sweep | 0x80000000u; }
 
 // Rule 0..3 (Julia rules 1..4) from the children kinds; -1 when both children are leaves.
 TSA_HD int pick_rule(bool li, bool ri, uint32_t r) {

@@ -419,6 +419,7 @@ struct tsa_session {
   // options (owned copies)
   std::vector<float> betas;
   int niters = 0, nchains = 0, scheme = 0, order = 0, eval_every = 1, slicing = 0, slice_moves = 0;
+  int par_band = 0, par_follow = 0;  // par-order variants (--par-band, --par-follow)
   int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1, exp_device = 0;
   double sc_target = 20, sc_weight = 1, trunc_frac = 0.25;
   uint64_t seed = 1;
@@ -518,7 +519,8 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
     CKR(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     s->own_stream = true;
   }
-  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, s->order, s->slice_moves, &s->plan) !=
+  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, s->order, s->slice_moves, s->par_follow,
+                       &s->plan) !=
       cudaSuccess) {
     set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
     return TSA_ERR_UNSUPPORTED;
@@ -695,6 +697,18 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   s->max_slices = O->max_slices > 0 ? O->max_slices : I.nlab;
   s->select_sc = O->select_sc ? 1 : 0;
   s->verbose = O->verbose;
+  if (O->par_band < 0 || O->par_band == 1 || O->par_band > 16) {
+    set_err(err, errlen, "--par-band L: 0 (off) or 2..16");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  s->par_band = O->order == TSA_ORDER_PAR ? O->par_band : 0;
+  s->par_follow = O->order == TSA_ORDER_PAR && O->par_follow ? 1 : 0;
+  if (O->kernel_hint == 3 && (s->par_band || s->par_follow)) {
+    set_err(err, errlen, "kernel_hint 3 (two warps per chain) runs plain par order (no par_band / par_follow)");
+    delete s;
+    return TSA_ERR_ARG;
+  }
   if (O->kernel_hint < 0 || O->kernel_hint > 4) {
     set_err(err, errlen, "kernel_hint must be 0 (auto), 1 (warp), 2 (block), 3 (pair of warps) or 4 (pair of CTAs)");
     delete s;
@@ -814,6 +828,8 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.exp_device = s->exp_device;
   a.leaf_sc = s->I.leaf_sc;
   a.slice_moves = s->slice_moves;
+  a.par_band = s->par_band;
+  a.par_follow = s->par_follow;
   a.slice_every = s->slice_every;
   a.max_slices = s->max_slices;
   a.stats = s->d_stats;

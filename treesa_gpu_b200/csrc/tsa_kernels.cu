@@ -8,8 +8,16 @@
 // and the per-chain energy (reference k_energy, :1000-1014) is fused into the same launch, read from
 // the per-node (cost, size) cache instead of a second pass over the label sets.
 //
-// k_anneal_block: one CTA per chain for chains too large for shared memory (the 64x64 lattice: 4 MB);
-// per-node metadata in shared memory, label sets streamed from HBM with 16-byte loads, G lanes per node.
+// ORDER 0 is par order, 1 pre-order, 2 par order with the --par-band / --par-follow variants (its own
+// instantiation, so that plain par order keeps its registers).
+//
+// k_anneal_block: one CTA per chain for chains too large for shared memory; per-node metadata in shared
+// memory, label sets streamed from HBM in 16-byte chunks: par phases with chunk summaries as flat
+// (node, chunk) item lists spread over all threads (par_phase_flat), otherwise G lanes per node.
+//
+// k_anneal_cluster: par order with chunk summaries when chains are fewer than half the SMs (the 64x64
+// lattice: 72 chains of 4 MB): a cluster of two CTAs per chain, metadata replicated in both CTAs'
+// shared memory and kept equal by distributed-shared-memory stores, one cluster barrier per phase.
 //
 // Every kernel produces bit-identical trees to the reference's CPU port (csrc/cpu_ref.h) for the same
 // Philox counters; see tsa_core.h for the arithmetic.
@@ -431,6 +439,71 @@ __device__ void slice_step(const WarpCtx& X_, const SweepArgs& a, uint64_t* lab,
 }
 
 // ------------------------------------------------------------------------------------------------
+// Depth of every internal node (root 0) by pointer jumping: word i = depth << 16 | ancestor (0xFFFF once
+// the root is reached); every round adds the ancestor's depth and jumps to the ancestor's ancestor, so
+// log2(depth) + 1 rounds suffice.  Two buffers of nint words; the result ends in A.  One warp.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void warp_depths(const uint16_t* par, int m, int nint, uint32_t*& A, uint32_t*& Bq,
+                                            int lane) {
+  for (int i = lane; i < nint; i += 32) {
+    const int p = par[i];
+    A[i] = p == 0xFFFF ? 0xFFFFu : ((1u << 16) | (uint32_t)(p - m));
+  }
+  __syncwarp();
+  for (int r = 0; r < 18; r++) {
+    bool more = false;
+    for (int i = lane; i < nint; i += 32) {
+      uint32_t x = A[i];
+      const uint32_t an = x & 0xFFFFu;
+      if (an < (uint32_t)nint) {  // 0xFFFF: the root is reached
+        const uint32_t y = A[an];
+        x = (((x >> 16) + (y >> 16)) << 16) | (y & 0xFFFFu);
+        more |= (y & 0xFFFFu) != 0xFFFFu;
+      }
+      Bq[i] = x;
+    }
+    __syncwarp();
+    uint32_t* t = A;
+    A = Bq;
+    Bq = t;
+    if (!__any_sync(0xFFFFFFFFu, more)) break;
+  }
+}
+
+// The same over a CTA; the result ends in the buffer U32 (which the caller then reads while it
+// overwrites the other one).
+__device__ __forceinline__ void block_depths(const uint16_t* par, int m, int nint, uint32_t* A0, uint32_t* U32) {
+  const int tid = threadIdx.x, T = blockDim.x;
+  uint32_t *A = A0, *Bq = U32;
+  for (int i = tid; i < nint; i += T) {
+    const int p = par[i];
+    A[i] = p == 0xFFFF ? 0xFFFFu : ((1u << 16) | (uint32_t)(p - m));
+  }
+  __syncthreads();
+  for (int r = 0; r < 18; r++) {
+    bool more = false;
+    for (int i = tid; i < nint; i += T) {
+      uint32_t x = A[i];
+      const uint32_t an = x & 0xFFFFu;
+      if (an < (uint32_t)nint) {  // 0xFFFF: the root is reached
+        const uint32_t y = A[an];
+        x = (((x >> 16) + (y >> 16)) << 16) | (y & 0xFFFFu);
+        more |= (y & 0xFFFFu) != 0xFFFFu;
+      }
+      Bq[i] = x;
+    }
+    uint32_t* t = A;
+    A = Bq;
+    Bq = t;
+    if (!__syncthreads_or(more)) break;
+  }
+  if (A != U32) {
+    for (int i = tid; i < nint; i += T) U32[i] = A[i];
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // k_anneal_warp: nsweeps sweeps of every chain, one warp per chain, chains in shared memory.
 // ------------------------------------------------------------------------------------------------
 template <int NW, int ORDER>
@@ -504,7 +577,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
     __syncwarp();
     const uint32_t chain = (uint32_t)(a.chain0 + c);
     const uint32_t hc = chain_hash(chain, a.key0);
-    if (ORDER == 0) {
+    if (ORDER != 1) {
       for (int i = lane; i < nint; i += 32) {
         uint32_t cw = ch[i];
         int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
@@ -517,20 +590,53 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
     Set<NW> NM = not_sliced<NW>(S, X_.slicing);
     for (int s = 0; s < a.nsweeps; s++) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
-      if (ORDER == 0) {
+      if (ORDER != 1) {
         // ---- par order: phases of independent sets (cpu_ref.h:133-182, k_par :897-972) ----
         // key[i] = priority << 16 | node id while node m+i is unvisited, 0 once visited; key[nint] = 0 is
         // the sentinel read for a leaf child or the root's parent, so a node is active iff its key
         // exceeds the keys of its parent and children.
         const uint32_t hs = sweep_hash(sw, hc);
-        for (int i = lane; i < nint; i += 32) {
-          key[i] = (node_pri((uint32_t)(m + i), hs) << 16) | (uint32_t)(m + i);
-          U[i] = (uint16_t)i;
+        if (ORDER == 2 && a.par_band > 0) {
+          // depth of every node at the start of the sweep, by pointer jumping over two buffers that are
+          // free until the priorities are set: key[] and the wl/U lists (read as u32)
+          uint32_t* A = key;
+          uint32_t* Bq = reinterpret_cast<uint32_t*>(wl);
+          warp_depths(par, m, nint, A, Bq, lane);
+          // A now holds depth << 16 (| 0xFFFF): each lane reads and rewrites only its own nodes' words
+          for (int i = lane; i < nint; i += 32)
+            key[i] = (band_pri(node_pri((uint32_t)(m + i), hs), (int)(A[i] >> 16), a.par_band) << 16) |
+                     (uint32_t)(m + i);
+          __syncwarp();
+          for (int i = lane; i < nint; i += 32) U[i] = (uint16_t)i;
+        } else {
+          for (int i = lane; i < nint; i += 32) {
+            key[i] = (node_pri((uint32_t)(m + i), hs) << 16) | (uint32_t)(m + i);
+            U[i] = (uint16_t)i;
+          }
         }
         if (lane == 0) key[nint] = 0u;
         int nU = nint;
         __syncwarp();
-        for (int guard = 0; guard <= nint; guard++) {
+        // par_follow: an accepted first visit (odd priority) re-arms its pivot child P with an even
+        // priority if the sweep already visited it; P goes back on the unvisited list, and its second
+        // visit draws Philox with the sweep's top bit set (cpu_ref.h:168-175)
+        const bool follow = ORDER == 2 && a.par_follow != 0;
+        auto swv = [&](uint32_t k) { return ((k >> 16) & 1u) ? sw : follow_sweep(sw); };
+        auto rearm = [&](const Prop<NW>& p, uint32_t k) -> int {
+          if (!follow || !p.acc || !((k >> 16) & 1u)) return -1;
+          const int pi = p.Pn - m;
+          if (key[pi] != 0u) return -1;
+          key[pi] = (follow_pri((uint32_t)p.Pn, hs) << 16) | (uint32_t)p.Pn;
+          return pi;
+        };
+        auto push = [&](int r0, int r1) {  // re-armed nodes onto the unvisited list (all lanes)
+          const unsigned b0 = __ballot_sync(FULL, r0 >= 0), b1 = __ballot_sync(FULL, r1 >= 0);
+          if (r0 >= 0) U[nU + __popc(b0 & lt)] = (uint16_t)r0;
+          if (r1 >= 0) U[nU + __popc(b0) + __popc(b1 & lt)] = (uint16_t)r1;
+          nU += __popc(b0) + __popc(b1);
+        };
+        const int max_phases = follow ? 2 * nint : nint;
+        for (int guard = 0; guard <= max_phases; guard++) {
           int nk = 0, nu = 0, nc = 0;
           // two list entries per lane per step: their shared-memory loads overlap
           for (int base = 0; base < nU; base += 64) {
@@ -577,9 +683,9 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
             const int ja = j, jb = j + 32;
             const bool vb = jb < nk;
             const int ia = wl[ja], ib = vb ? (int)wl[jb] : ia;
-            const uint32_t cha = ch[ia], chb = ch[ib];
-            Prop<NW> pa = propose<NW>(X_, lab, ch, cz, NM, m + ia, cha, sw, chain);
-            Prop<NW> pb = propose<NW>(X_, lab, ch, cz, NM, m + ib, chb, sw, chain);
+            const uint32_t cha = ch[ia], chb = ch[ib], ka = key[ia], kb = key[ib];
+            Prop<NW> pa = propose<NW>(X_, lab, ch, cz, NM, m + ia, cha, swv(ka), chain);
+            Prop<NW> pb = propose<NW>(X_, lab, ch, cz, NM, m + ib, chb, swv(kb), chain);
             cnt.prop += 1 + vb;
             cnt.acc += pa.acc + (vb && pb.acc);
             cnt.visits += 1 + vb;
@@ -587,13 +693,23 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
             if (vb && pb.acc) apply<NW, true>(pb, m, lab, ch, cz, par);
             key[ia] = 0u;
             if (vb) key[ib] = 0u;
+            if (follow) push(rearm(pa, ka), vb ? rearm(pb, kb) : -1);
           }
+          int ra = -1;
           if (j < nk) {
             const int i = wl[j];
-            visit<NW, true>(X_, lab, ch, cz, NM, par, m + i, sw, chain, cnt);
-            key[i] = 0u;
+            const uint32_t ki = key[i];
+            Prop<NW> p = propose<NW>(X_, lab, ch, cz, NM, m + i, ch[i], swv(ki), chain);
+            cnt.prop++;
             cnt.visits++;
+            if (p.acc) {
+              cnt.acc++;
+              apply<NW, true>(p, m, lab, ch, cz, par);
+            }
+            key[i] = 0u;
+            ra = rearm(p, ki);
           }
+          if (follow) push(ra, -1);
           cnt.busy += nk;
           __syncwarp();
         }
@@ -940,9 +1056,11 @@ struct BlockSmem {
     if (L.sums) o += 8 * n2;
     b.off_S = rnd_up(o, 16);
     o = b.off_S + rnd_up(8u * (uint32_t)L.nw, 16);
-    b.off_pri = o;
-    o += 2 * n2;
+    // pri and wl are adjacent, and so are U and U2: read as two arrays of n2 words they hold the depth
+    // computation of par_band at the start of a sweep
     b.off_par = o;
+    o += 2 * n2;
+    b.off_pri = o;
     o += 2 * n2;
     b.off_wl = o;
     o += 2 * n2;
@@ -1046,9 +1164,27 @@ __device__ __forceinline__ void for_chunks(uint64_t u, int nchunks, int G, int t
   }
 }
 
+// par_follow state of a CTA's sweep: an accepted first visit re-arms its pivot child P (if the sweep
+// already visited it) with an even priority and appends P to the unvisited list U at *nU
+// (cpu_ref.h:168-175).
+struct FollowCtx {
+  uint16_t* pri;
+  uint16_t* U;
+  int* nU;
+  uint32_t hs;
+};
+__device__ __forceinline__ void follow_rearm(const FollowCtx* f, int Pn, int m) {
+  if (f && f->pri[Pn - m] == 0) {
+    f->pri[Pn - m] = (uint16_t)follow_pri((uint32_t)Pn, f->hs);
+    f->U[atomicAdd(f->nU, 1)] = (uint16_t)(Pn - m);
+  }
+}
+
+// sweep: the Philox sweep counter of this visit; fol: re-arm on accept (a first visit with par_follow)
 template <bool SUMS, bool PAR>
 __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
-                                           int G, int t, unsigned gm, Counters& cnt) {
+                                           int G, int t, unsigned gm, Counters& cnt,
+                                           const FollowCtx* fol = nullptr) {
   const int m = B.m, i = v - m, nw = B.nw;
   uint32_t chv = B.ch[i];
   int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
@@ -1126,6 +1262,7 @@ __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v
       if (On >= m) par[On - m] = (uint16_t)Pn;
       if (Mn >= m) par[Mn - m] = (uint16_t)v;
     }
+    follow_rearm(fol, Pn, m);
   }
 }
 
@@ -1421,7 +1558,8 @@ __device__ __forceinline__ void flat_store(const BlkCtx& B, const FlatTabs& F, I
 // CL = 2: one CTA of a pair; metadata writes go to both CTAs' copies (P: the other CTA's arrays).
 template <bool PAR, int CL>
 __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl, uint16_t* pri, uint16_t* par,
-                               int nk, uint32_t sweep, uint32_t chain, Counters& cnt, const PeerArrays& P) {
+                               int nk, uint32_t sweep, uint32_t chain, Counters& cnt, const PeerArrays& P,
+                               const FollowCtx* fol = nullptr) {
   const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31, warp = tid >> 5, nwarps = T >> 5;
   const int m = B.m;
   const int NB = min(kFlatBatch, T);  // owners are threads 0..NB-1
@@ -1430,18 +1568,19 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     const uint16_t* wlb = wl + b0;
     // 1. owners: rule, pivot and chunk union
     int q = 0, nck = 0;
-    bool prop = false;
+    bool prop = false, first = true;
     uint32_t chv = 0;
     if (tid < nb) {
       q = wlb[tid];
       chv = B.ch[q];
+      first = (pri[q] & 1u) != 0;  // an even priority marks a follow-up visit
       const int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
       const bool li = l >= m, ri = r >= m;
       prop = li || ri;
       uint2 inf = make_uint2(0xFFFFFFFFu, 0xFFFFFFFFu);
       uint64_t u = 0;
       if (prop) {
-        const U4 rnd = philox10((uint32_t)(m + q), sweep, chain, 0u, B.key0, B.key1);
+        const U4 rnd = philox10((uint32_t)(m + q), first ? sweep : follow_sweep(sweep), chain, 0u, B.key0, B.key1);
         const int rule = pick_rule(li, ri, rnd.x);
         const int slotP = rule >> 1, slotM = ((rule ^ (rule >> 1)) & 1) ^ 1;
         const int Pn = slotP ? r : l, On = slotP ? l : r;
@@ -1547,6 +1686,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
             if (On >= m) mset<uint16_t>(par, P.par, On - m, (uint16_t)Pn);
             if (Mn >= m) mset<uint16_t>(par, P.par, Mn - m, (uint16_t)(m + q));
           }
+          if (first) follow_rearm(fol, Pn, m);  // fol is null for a CTA pair
         }
       }
       F.acc[tid] = acc;
@@ -1667,13 +1807,25 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
       if (ORDER == 0) {
         const uint32_t hs = sweep_hash(sw, hc);
-        for (int q = tid; q < nint; q += T) {
-          pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
-          Ua[q] = (uint16_t)q;
+        if (a.par_band > 0) {
+          // depths at the start of the sweep in (pri, wl) and (U, U2) read as word arrays
+          uint32_t* U32 = reinterpret_cast<uint32_t*>(Ua);
+          block_depths(par, m, nint, reinterpret_cast<uint32_t*>(pri), U32);
+          for (int q = tid; q < nint; q += T)
+            pri[q] = (uint16_t)band_pri(node_pri((uint32_t)(m + q), hs), (int)(U32[q] >> 16), a.par_band);
+          __syncthreads();
+          for (int q = tid; q < nint; q += T) Ua[q] = (uint16_t)q;
+        } else {
+          for (int q = tid; q < nint; q += T) {
+            pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
+            Ua[q] = (uint16_t)q;
+          }
         }
         uint16_t *U = Ua, *U2 = Ub;
         int nU = nint;
-        for (int guard = 0; guard <= nint; guard++) {
+        const bool follow = a.par_follow != 0;
+        const int max_phases = follow ? 2 * nint : nint;
+        for (int guard = 0; guard <= max_phases; guard++) {
           if (tid == 0) {
             sh[0] = 0;
             sh[1] = 0;
@@ -1722,15 +1874,20 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
           U2 = tmp;
           if (nk == 0) break;
           if (tid == 0) cnt.steps++;
+          // re-armed pivots (par_follow) are appended to U after the nU kept nodes, counted on in sh[1]
+          const FollowCtx fctx{pri, U, &sh[1], hs};
+          const FollowCtx* fol = follow ? &fctx : nullptr;
           if constexpr (SUMS) {
-            par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{});
+            par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{}, fol);
           } else {
             const int G = pick_group(nk, T);
             const int groups = T / G, g = tid / G, t = tid & (G - 1);
             const unsigned gm = G == 32 ? FULL : (((1u << G) - 1u) << (lane & ~(G - 1)));
             for (int j = g; j < nk; j += groups) {
               int q = wl[j];
-              visit_coop<SUMS, true>(B, par, m + q, sw, chain, G, t, gm, cnt);
+              const bool first = (pri[q] & 1u) != 0;  // an even priority marks a follow-up visit
+              visit_coop<SUMS, true>(B, par, m + q, first ? sw : follow_sweep(sw), chain, G, t, gm, cnt,
+                                     first ? fol : nullptr);
               if (t == 0) {
                 pri[q] = 0;
                 cnt.visits++;
@@ -1738,6 +1895,10 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
               cnt.busy++;
             }
             __syncthreads();
+          }
+          if (follow) {
+            nU = sh[1];
+            __syncthreads();  // every thread has read the count before the next phase clears it
           }
         }
       } else {
@@ -1920,13 +2081,22 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
     }
     if (tid == 0) par[nint - 1] = 0xFFFFu;
     for (int q = tid; q < L.nw; q += T) B.S[q] = gS[q];
+    __syncthreads();  // the copy is complete before any thread reads it (par_band reads par first)
     const uint32_t chain = (uint32_t)(a.chain0 + c);
     const uint32_t hc = chain_hash(chain, a.key0);
     int ph = 0;  // phases of this chain: parity selects the exchange slot
     for (int s = 0; s < a.nsweeps; s++) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
       const uint32_t hs = sweep_hash(sw, hc);
-      for (int q = tid; q < nint; q += T) pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
+      if (a.par_band > 0) {  // both CTAs compute the same depths from their identical copies
+        uint32_t* U32 = reinterpret_cast<uint32_t*>(Ua);
+        block_depths(par, m, nint, reinterpret_cast<uint32_t*>(pri), U32);
+        for (int q = tid; q < nint; q += T)
+          pri[q] = (uint16_t)band_pri(node_pri((uint32_t)(m + q), hs), (int)(U32[q] >> 16), a.par_band);
+        __syncthreads();
+      } else {
+        for (int q = tid; q < nint; q += T) pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
+      }
       int nU = (nint - rank + 1) / 2;  // the nodes q = 2j + rank
       for (int j = tid; j < nU; j += T) Ua[j] = (uint16_t)(2 * j + rank);
       uint16_t *U = Ua, *U2 = Ub;
@@ -2075,6 +2245,7 @@ static cudaError_t launch_pair(const SweepArgs& a, const LaunchPlan& p, cudaStre
 }
 
 template <int ORDER>
+// ORDER: 0 par, 1 pre-order, 2 par with par_band / par_follow
 static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
   switch (a.L.nw) {
     case 1: return launch_warp_t<1, ORDER>(a, p, st);
@@ -2135,14 +2306,14 @@ static int cluster_capacity(size_t smem, int grid) {
 }
 
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
-                        LaunchPlan* plan) {
+                        int par_follow, LaunchPlan* plan) {
   int nsm = 0, optin = 0;
   cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   if (e != cudaSuccess) return e;
   bool warp_ok = (L.nw == 1 || L.nw == 2 || L.nw == 4 || L.nw == 6 || L.nw == 8) && hint != 2;
-  // par order: two warps per chain (up to 14 pairs per SM)
+  // par order: two warps per chain (up to 14 pairs per SM; plain par order only)
   if (warp_ok && order == 0 && hint == 3) {
     int np = 14;
     while (np > 0 && PairSmem::make(L, np, slice_moves).total > (uint32_t)optin) np--;
@@ -2191,7 +2362,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   plan->cluster = 1;
   // par order with chunk summaries and at most half as many chains as SMs: a pair of CTAs per chain,
   // if every pair can be resident at once
-  const bool pair_ok = L.sums && order == 0 && slice_moves == 0;
+  const bool pair_ok = L.sums && order == 0 && slice_moves == 0 && !par_follow;
   if (hint == 4 && !pair_ok) return cudaErrorNotSupported;
   if (pair_ok && (hint == 4 || (hint == 0 && 2 * nchains <= nsm))) {
     const int grid = 2 * nchains;
@@ -2209,7 +2380,10 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
 
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
   if (p.kind == K_PAIR) return launch_pair(a, p, st);
-  if (p.kind == K_WARP) return a.order == 0 ? launch_warp_o<0>(a, p, st) : launch_warp_o<1>(a, p, st);
+  if (p.kind == K_WARP) {
+    if (a.order != 0) return launch_warp_o<1>(a, p, st);
+    return a.par_band || a.par_follow ? launch_warp_o<2>(a, p, st) : launch_warp_o<0>(a, p, st);
+  }
   if (p.cluster == 2) return launch_cluster(a, p, st);
   if (a.L.sums) return a.order == 0 ? launch_block_t<true, 0>(a, p, st) : launch_block_t<true, 1>(a, p, st);
   return a.order == 0 ? launch_block_t<false, 0>(a, p, st) : launch_block_t<false, 1>(a, p, st);

@@ -46,6 +46,8 @@ struct SweepArgs {
   int* err;                  // nonzero: a bounded wait timed out
   const float* lse_tab;      // 64 floats (device)
   const uint64_t* leaf_sum;  // [m] chunk summaries of the leaf sets (when L.sums)
+  int par_band;              // par order: 0, or L = 2..16 (priorities by depth band)
+  int par_follow;            // par order: re-visit the pivot child of an accepted first visit
 };
 
 // Kernel family chosen by the host for a layout.
@@ -63,7 +65,7 @@ struct LaunchPlan {
 // hint: 0 auto, 1 one warp per chain, 2 one CTA per chain (label sets in HBM), 3 two warps per chain,
 // 4 a pair of CTAs per chain (par order with chunk summaries, no slice moves)
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
-                        LaunchPlan* plan);
+                        int par_follow, LaunchPlan* plan);
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
                                cudaStream_t st);

@@ -8,8 +8,10 @@ an omeco-format dict with internal ``iy`` recomputed from the topology, ``info``
 binary's JSON result plus the Python recomputations (tc_py, sc_py, gpu_time_py, h100_time_py, totals over
 slices, wall, init).  Where the reference wrote temp files and spawned its CLI binary
 (driver.py:215-314), this calls ``tsa_run`` of libtreesa_b200.so through ctypes; there is no fallback path.
-Kernel-tuning keywords of the reference (kernel, wpb, block, lpc, coop_*, wpc, chunk_sums, wide,
-par_follow, par_band) are accepted; they never change a result here and are ignored.
+Kernel-tuning keywords of the reference (wpb, block, lpc, coop_*, wpc, chunk_sums, wide) are accepted; they
+never change a result, here or in the reference, and are ignored.  ``kernel`` keeps its meaning (anything
+but "auto"/"par" selects the pre-order sweep), and the par-order variants ``par_follow`` and ``par_band``
+(the CLI's --par-follow / --par-band, csrc/treesa_gpu.cu:1388-1389) run as in the reference.
 """
 import heapq
 import math
@@ -266,7 +268,8 @@ def optimize(ixs, iy, nchains=1024, betas=None, niters=50, sc_target=20.0, sc_we
                 init_slices=[lmap[l] for l in (init_slices or [])], select_sc=(select == "sc"),
                 init_trees=init_trees, gpu_model=[float(gm[k]) for k in GPU_KEYS],
                 h100_model=[float(h100m[k]) for k in H100_KEYS], device=0 if device is None else int(device),
-                verbose=verbose, rank=rank, world_size=world, nccl_id=nccl_id, stream=stream)
+                verbose=verbose, rank=rank, world_size=world, nccl_id=nccl_id, stream=stream,
+                par_follow=bool(par_follow), par_band=int(par_band or 0))
     t0 = time.time()
     rc, res = engine.run(net, **opts)
     wall = time.time() - t0
@@ -285,7 +288,8 @@ def optimize(ixs, iy, nchains=1024, betas=None, niters=50, sc_target=20.0, sc_we
     t2 = trees.tree_h100_time(tree, ixs_s, h100m)
     info.update(sliced=sliced, tc_py=tc, sc_py=sc, gpu_time_py=t1, h100_time_py=t2, tc_total_py=tc + len(sliced),
                 h100_time_total_py=t2 * 2.0 ** len(sliced), wall=wall, t_greedy=t_greedy, tmpdir=None,
-                init_tcs=spectral_tcs, init=init)
+                init_tcs=spectral_tcs, init=init, par_follow=int(bool(par_follow) and order == "par"),
+                par_band=int(par_band or 0) if order == "par" else 0)
     return tree, info
 
 
