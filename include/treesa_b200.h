@@ -93,7 +93,13 @@ typedef struct tsa_options {
                                  re-visits its pivot child later in the sweep if the sweep already visited it */
   int32_t par_band;           /* --par-band L (:1389): 0 off, or 2..16: par-order priorities top-down within
                                  bands of L levels of the depth at the start of each sweep */
-  int32_t reserved[10];
+  /* Stage 2 (--stage2-betas/--stage2-niters/--stage2-mode, :1281-1296, 1354-1357; the driver's modes
+     "tc+gpu"/"tc+h100"): after the nbetas levels, continue the population on betas2 in mode2 */
+  int32_t mode2;              /* TSA_MODE_GPU or TSA_MODE_H100 */
+  int32_t niters2;            /* sweeps per level of stage 2 (<= 0: niters) */
+  const float* betas2;        /* NULL: no stage 2 */
+  int32_t nbetas2;
+  int32_t reserved[7];
 } tsa_options;
 
 /* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the

@@ -43,7 +43,8 @@ def orc():
                               C.c_size_t]
         L.orc_result_free.argtypes = [C.POINTER(_abi.Result)]
         L.orc_result_free.restype = None
-        L.orc_sweeps.argtypes = [C.POINTER(_abi.Instance), C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_double, C.c_double,
+        L.orc_sweeps.argtypes = [C.POINTER(_abi.Instance), C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_double,
+                                 C.c_double,
                                  C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_uint32),
                                  C.POINTER(C.c_uint64), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
                                  C.POINTER(C.c_longlong), C.c_char_p, C.c_size_t]
@@ -74,7 +75,7 @@ def cpuref():
                                  C.c_double, C.c_double, C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int, C.c_int,
                                  C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
                                  C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.POINTER(C.c_longlong), C.c_int,
-                                 C.c_int, C.c_int]
+                                 C.c_int, C.c_int, C.c_int]
         L.ref_max_threads.restype = C.c_int
         _REF = L
     return _REF
@@ -152,7 +153,7 @@ def energy(net, tree, S=None):
 
 
 def sweeps(net, trees, betas, niters, order="par", seed=1, sc_target=20.0, sc_weight=1.0, c0=0, S=None,
-           par_band=0, par_follow=False):
+           par_band=0, par_follow=False, mode="tc"):
     """Our restatement: final (trees, labels, counters) after the schedule (sweep ids lev*niters+it)."""
     trees = np.ascontiguousarray(trees, np.uint32)
     nch = trees.shape[0]
@@ -165,7 +166,7 @@ def sweeps(net, trees, betas, niters, order="par", seed=1, sc_target=20.0, sc_we
         S = np.ascontiguousarray(S, np.uint64)
         Sp = _p(S, C.c_uint64)
     err = C.create_string_buffer(256)
-    rc = orc().orc_sweeps(C.byref(net.inst), _abi.ORDER[order], int(par_band), int(bool(par_follow)), seed,
+    rc = orc().orc_sweeps(C.byref(net.inst), _abi.ORDER[order], int(par_band), int(bool(par_follow)), _abi.MODE[mode], seed,
                           sc_target, sc_weight, _p(betas, C.c_float),
                           len(betas), niters, nch, c0, _p(trees, C.c_uint32), Sp, _p(tout, C.c_uint32),
                           _p(lout, C.c_uint64), _p(cnt, C.c_longlong), err, 256)
@@ -175,7 +176,7 @@ def sweeps(net, trees, betas, niters, order="par", seed=1, sc_target=20.0, sc_we
 
 
 def ref_sweeps(net, trees, betas, niters, order="par", seed=1, sc_target=20.0, sc_weight=1.0, c0=0, S=None,
-               nthreads=0, par_band=0, par_follow=False):
+               nthreads=0, par_band=0, par_follow=False, mode="tc"):
     """The reference's cpu_ref.h: final (trees, labels, counters, seconds)."""
     L = cpuref()
     if L is None:
@@ -195,5 +196,5 @@ def ref_sweeps(net, trees, betas, niters, order="par", seed=1, sc_target=20.0, s
     secs = L.ref_sweeps(net.m, net.nlab, _p(net.off, C.c_int), _p(net.flat, C.c_int), _abi.ORDER[order], seed,
                         sc_target, sc_weight, _p(betas, C.c_float), len(betas), niters, nch, c0,
                         _p(trees, C.c_uint32), _p(lin, C.c_uint64), Sp, _p(tout, C.c_uint32), _p(lout, C.c_uint64),
-                        _p(cnt, C.c_longlong), nthreads, int(par_band), int(bool(par_follow)))
+                        _p(cnt, C.c_longlong), nthreads, int(par_band), int(bool(par_follow)), _abi.MODE[mode])
     return tout, lout, cnt, secs

@@ -38,11 +38,12 @@ extern "C" {
 // the internal nodes' output labels) and slice sets S_in ([nch][nw64] or NULL), nbetas levels of
 // niters sweeps each; order 0 = par, 1 = preorder.  Writes trees_out / labels_out (labels_out may be
 // NULL); counters = {proposals, accepts}; par_band / par_follow as the CLI's --par-band / --par-follow
-// (treesa_gpu.cu:1388-1389, 1524-1527); returns the seconds spent in the sweep loops.
+// (treesa_gpu.cu:1388-1389, 1524-1527); mode 0 tc, 1 gpu model, 2 h100 model (default constants);
+// returns the seconds spent in the sweep loops.
 double ref_sweeps(int m, int nlab, const int* ix_off, const int* ix_lab, int order, uint64_t seed, double sc_target,
                   double sc_weight, const float* betas, int nbetas, int niters, int nch, int c0,
                   const uint32_t* trees_in, const uint64_t* labels_in, const uint64_t* S_in, uint32_t* trees_out,
-                  uint64_t* labels_out, long long* counters, int nthreads, int par_band, int par_follow) {
+                  uint64_t* labels_out, long long* counters, int nthreads, int par_band, int par_follow, int mode) {
   fill_table();
   const int nw = (nlab + 63) / 64 > 0 ? (nlab + 63) / 64 : 1, nint = m - 1;
   Params P{};
@@ -52,6 +53,27 @@ double ref_sweeps(int m, int nlab, const int* ix_off, const int* ix_lab, int ord
   P.sc_weight = (float)sc_weight;
   P.par_band = par_band;
   P.par_follow = par_follow;
+  // the default gpu / h100 model constants, as the reference's Runner sets Params from them
+  // (treesa_gpu.cu:1460-1475, defaults of treesa_gpu/driver.py / trees.py)
+  {
+    const double gm[6] = {11.9e15, 1.6e13, 6, 6, 8, 4e-6};
+    const double hm[9] = {4e-6, 1.23e13, 5.44e-14, 7.68e-15, 6.37e-14, 2.02e-16, 1.77e-13, 14, 1e-12};
+    P.lpeak = (float)std::log2(gm[0]);
+    P.lbw = (float)std::log2(gm[1]);
+    P.m0 = (int)gm[2];
+    P.n0 = (int)gm[3];
+    P.k0 = (int)gm[4];
+    P.llaunch = (float)std::log2(gm[5]);
+    P.v2_l3launch = (float)std::log2(3 * hm[0]);
+    P.v2_lperm2 = (float)std::log2(2 / hm[1]);
+    P.v2_lcc_bit = (float)std::log2(hm[2]);
+    P.v2_lcc_cell = (float)std::log2(hm[3]);
+    P.v2_ltc_bit = (float)std::log2(hm[4]);
+    P.v2_ltc_pad = (float)std::log2(hm[5]);
+    P.v2_ltc_out = (float)std::log2(hm[6]);
+    P.v2_small_rank = (int)hm[7];
+    P.v2_lsmall_cell = (float)std::log2(hm[8]);
+  }
   uint64_t k = splitmix64_h(seed);
   P.key0 = (uint32_t)k;
   P.key1 = (uint32_t)(k >> 32);
@@ -87,8 +109,16 @@ double ref_sweeps(int m, int nlab, const int* ix_off, const int* ix_lab, int ord
       for (int lev = 0; lev < nbetas; lev++)
         for (int it = 0; it < niters; it++) {
           uint32_t sw = (uint32_t)(lev * niters + it);
-          if (order == 0) ref_par_sweep<0>(T, betas[lev], sw, (uint32_t)(c0 + q), P, a, b);
-          else ref_optimize_subtree<0>(T, 2 * m - 2, betas[lev], sw, (uint32_t)(c0 + q), P, a, b);
+          const uint32_t ch = (uint32_t)(c0 + q);
+          if (order == 0) {
+            if (mode == 1) ref_par_sweep<1>(T, betas[lev], sw, ch, P, a, b);
+            else if (mode == 2) ref_par_sweep<2>(T, betas[lev], sw, ch, P, a, b);
+            else ref_par_sweep<0>(T, betas[lev], sw, ch, P, a, b);
+          } else {
+            if (mode == 1) ref_optimize_subtree<1>(T, 2 * m - 2, betas[lev], sw, ch, P, a, b);
+            else if (mode == 2) ref_optimize_subtree<2>(T, 2 * m - 2, betas[lev], sw, ch, P, a, b);
+            else ref_optimize_subtree<0>(T, 2 * m - 2, betas[lev], sw, ch, P, a, b);
+          }
         }
       double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
       secs = dt > secs ? dt : secs;

@@ -252,12 +252,81 @@ bool labels_from_topology(const Inst& I, const uint32_t* ch, uint64_t* lab) {
   return true;
 }
 
+struct Models {
+  float lpeak, lbw, llaunch;
+  int m0, n0, k0;
+  float l3launch, lperm2, lcc_bit, lcc_cell, ltc_bit, ltc_pad, ltc_out, lsmall_cell;
+  int small_rank;
+};
+Models make_models(const double* gm_in, const double* hm_in) {  // Runner ctor, treesa_gpu.cu:1461-1475
+  const double gm_def[6] = {11.9e15, 1.6e13, 6, 6, 8, 4e-6};
+  const double hm_def[9] = {4e-6, 1.23e13, 5.44e-14, 7.68e-15, 6.37e-14, 2.02e-16, 1.77e-13, 14, 1e-12};
+  const double* gm = gm_in ? gm_in : gm_def;
+  const double* hm = hm_in ? hm_in : hm_def;
+  Models M;
+  M.lpeak = (float)log2(gm[0]);
+  M.lbw = (float)log2(gm[1]);
+  M.m0 = (int)gm[2], M.n0 = (int)gm[3], M.k0 = (int)gm[4];
+  M.llaunch = (float)log2(gm[5]);
+  M.l3launch = (float)log2(3 * hm[0]);
+  M.lperm2 = (float)log2(2 / hm[1]);
+  M.lcc_bit = (float)log2(hm[2]);
+  M.lcc_cell = (float)log2(hm[3]);
+  M.ltc_bit = (float)log2(hm[4]);
+  M.ltc_pad = (float)log2(hm[5]);
+  M.ltc_out = (float)log2(hm[6]);
+  M.small_rank = (int)hm[7];
+  M.lsmall_cell = (float)log2(hm[8]);
+  return M;
+}
+// Log-domain model costs of one pairwise contraction with label counts B, M, N, K (common.h:128-152),
+// float with the host libm's log2f/exp2f through lse_f, as the reference's CPU port evaluates them.
+float gpu_lt(int B, int M, int N, int K, const Models& P) {
+  int Me = M > P.m0 ? M : P.m0, Ne = N > P.n0 ? N : P.n0, Ke = K > P.k0 ? K : P.k0;
+  volatile float lops = (float)(1 + B + Me + Ne + Ke) - P.lpeak;
+  volatile float lbits = lse_f(lse_f((float)(B + M + K), (float)(B + N + K)), (float)(B + M + N)) - P.lbw;
+  float lt = lops > lbits ? lops : lbits;
+  return lse_f(lt, P.llaunch);
+}
+float h100_lt(int B, int M, int N, int K, const Models& P) {
+  if (B + M + N <= P.small_rank) {
+    volatile float r = P.lsmall_cell + (float)(B + M + N + K);
+    return r;
+  }
+  float la = (float)(B + M + K), lb = (float)(B + N + K), lc = (float)(B + M + N);
+  float lab = lse_f(la, lb), lmoved = lse_f(lab, lc);
+  volatile float perm = P.lperm2 + lab;
+  volatile float cb = P.lcc_bit + lmoved, cc = P.lcc_cell + (float)(B + M + N + K);
+  float best = lse_f(cb, cc);
+  int MN = M > N ? M : N;
+  if (K >= 7 && MN >= 5) {
+    int Me = M > 6 ? M : 6, Ne = N > 6 ? N : 6, Ke = K > 8 ? K : 8;
+    volatile float tb = P.ltc_bit + lmoved, tp = P.ltc_pad + (float)(B + Me + Ne + Ke), to = P.ltc_out + lc;
+    float tc = lse_f(lse_f(tb, tp), to);
+    best = tc < best ? tc : best;
+  }
+  return lse_f(lse_f(P.l3launch, perm), best);
+}
+// count3 of common.h:172-177 on one masked word: x, y -> z
+inline void count3(uint64_t x, uint64_t y, uint64_t z, int& B, int& M, int& N, int& K) {
+  B += __builtin_popcountll(x & y & z);
+  M += __builtin_popcountll(x & ~y & z);
+  N += __builtin_popcountll(~x & y & z);
+  K += __builtin_popcountll(x & y & ~z);
+}
+
 struct Par {
   int m, nint, nw, leaf_sc, slicing, slice_moves, slice_every, max_slices;
   float sc_target, sc_weight;
   uint32_t key0, key1;
   int par_band, par_follow;  // par-order variants (off: 0)
+  int mode;                  // energy: 0 tc, 1 gpu model, 2 h100 model
+  Models mo;
 };
+// log2 cost of the contraction (x, y) -> z in mode 1 or 2 (node_cost, common.h:158-162)
+inline float model_cost(const Par& P, int B, int M, int N, int K) {
+  return P.mode == 1 ? gpu_lt(B, M, N, K, P.mo) : h100_lt(B, M, N, K, P.mo);
+}
 
 inline const uint64_t* set_of(const Inst& I, const Chain& C, int v) {
   return v < I.m ? &I.leaf[(size_t)v * I.nw] : &C.lab[(size_t)(v - I.m) * I.nw];
@@ -307,6 +376,20 @@ bool visit(const Inst& I, const Par& P, Chain& C, int v, float beta, uint32_t sw
   }
   tcl += scl, tcr += scr, tcl1 += scl1, tcr1 += scr1;
   float tc0 = lse_i(tcl, tcr), tc1 = lse_i(tcl1, tcr1);
+  if (P.mode != 0) {  // cpu_ref.h:69-72: the four contractions (a,b)->ab, (ab,c)->d, (a,c)->ac, (ac,b)->d
+    int c[4][4] = {};
+    for (int w = 0; w < nw; w++) {
+      uint64_t nm = P.slicing ? ~S[w] : ~0ull;
+      uint64_t ma = A[w] & nm, mb = B[w] & nm, mab = AB[w] & nm, mc = Cc[w] & nm, md = D[w] & nm, mx = ac[w] & nm;
+      count3(ma, mb, mab, c[0][0], c[0][1], c[0][2], c[0][3]);
+      count3(mab, mc, md, c[1][0], c[1][1], c[1][2], c[1][3]);
+      count3(ma, mc, mx, c[2][0], c[2][1], c[2][2], c[2][3]);
+      count3(mx, mb, md, c[3][0], c[3][1], c[3][2], c[3][3]);
+    }
+    auto cost = [&](int k) { return model_cost(P, c[k][0], c[k][1], c[k][2], c[k][3]); };
+    tc0 = lse_f(cost(0), cost(1));
+    tc1 = lse_f(cost(2), cost(3));
+  }
   int sc0 = std::max(scl, scr), sc1 = std::max(scl1, scr1);
   volatile float dtc = tc1 - tc0;
   int dsc = sc1 - sc0;
@@ -436,14 +519,14 @@ Eval eval_chain(const Inst& I, const Par& P, const Chain& C) {
     uint32_t cw = C.ch[i];
     const uint64_t *x = set_of(I, C, (int)(cw & 0xFFFFu)), *y = set_of(I, C, (int)(cw >> 16));
     const uint64_t* z = &C.lab[(size_t)i * nw];
-    int K = 0, Z = 0;
+    int Bc = 0, Mc = 0, Nc = 0, K = 0, Z = 0;
     for (int w = 0; w < nw; w++) {
       uint64_t nm = S ? ~S[w] : ~0ull;
       uint64_t zz = z[w] & nm;
-      K += popc((x[w] & nm) & (y[w] & nm) & ~zz);
+      count3(x[w] & nm, y[w] & nm, zz, Bc, Mc, Nc, K);
       Z += popc(zz);
     }
-    acc[lane] = lse_f(acc[lane], (float)(Z + K));
+    acc[lane] = lse_f(acc[lane], P.mode == 0 ? (float)(Z + K) : model_cost(P, Bc, Mc, Nc, K));
     if (Z > scl[lane]) scl[lane] = Z, cntl[lane] = 1;
     else if (Z == scl[lane]) cntl[lane]++;
   }
@@ -544,33 +627,6 @@ void slice_step(const Inst& I, const Par& P, Chain& C, float beta, uint32_t swee
 // ---------------------------------------------------------------------------------------------
 // Host double-precision energies and the slicer repair (treesa_gpu.cu:1182-1274)
 // ---------------------------------------------------------------------------------------------
-struct Models {
-  float lpeak, lbw, llaunch;
-  int m0, n0, k0;
-  float l3launch, lperm2, lcc_bit, lcc_cell, ltc_bit, ltc_pad, ltc_out, lsmall_cell;
-  int small_rank;
-};
-Models make_models(const double* gm_in, const double* hm_in) {  // Runner ctor, treesa_gpu.cu:1461-1475
-  const double gm_def[6] = {11.9e15, 1.6e13, 6, 6, 8, 4e-6};
-  const double hm_def[9] = {4e-6, 1.23e13, 5.44e-14, 7.68e-15, 6.37e-14, 2.02e-16, 1.77e-13, 14, 1e-12};
-  const double* gm = gm_in ? gm_in : gm_def;
-  const double* hm = hm_in ? hm_in : hm_def;
-  Models M;
-  M.lpeak = (float)log2(gm[0]);
-  M.lbw = (float)log2(gm[1]);
-  M.m0 = (int)gm[2], M.n0 = (int)gm[3], M.k0 = (int)gm[4];
-  M.llaunch = (float)log2(gm[5]);
-  M.l3launch = (float)log2(3 * hm[0]);
-  M.lperm2 = (float)log2(2 / hm[1]);
-  M.lcc_bit = (float)log2(hm[2]);
-  M.lcc_cell = (float)log2(hm[3]);
-  M.ltc_bit = (float)log2(hm[4]);
-  M.ltc_pad = (float)log2(hm[5]);
-  M.ltc_out = (float)log2(hm[6]);
-  M.small_rank = (int)hm[7];
-  M.lsmall_cell = (float)log2(hm[8]);
-  return M;
-}
 double gpu_time_d(int B, int M_, int N, int K, const Models& M) {  // treesa_gpu.cu:1182-1186
   double ops = exp2((double)(1 + B + std::max(M_, M.m0) + std::max(N, M.n0) + std::max(K, M.k0)));
   double bits = exp2((double)(B + M_ + K)) + exp2((double)(B + N + K)) + exp2((double)(B + M_ + N));
@@ -682,6 +738,8 @@ Par make_par(const Inst& I, const tsa_options* O) {  // Runner ctor, treesa_gpu.
   P.sc_weight = (float)O->sc_weight;
   P.par_band = O->par_band;
   P.par_follow = O->par_follow ? 1 : 0;
+  P.mode = O->mode;
+  P.mo = make_models(O->gpu_model, O->h100_model);
   uint64_t k = splitmix64(O->seed);
   P.key0 = (uint32_t)k;
   P.key1 = (uint32_t)(k >> 32);
@@ -709,19 +767,24 @@ int orc_run(const tsa_instance* inst, const tsa_options* O, tsa_result* res, cha
   memset(res, 0, sizeof *res);
   Inst I;
   if (!load_instance(inst, I, err, errlen)) return TSA_ERR_ARG;
-  if (O->mode != TSA_MODE_TC) {
-    snprintf(err, errlen, "oracle: only mode tc");
-    return TSA_ERR_UNSUPPORTED;
-  }
   if (O->nchains < 1 || O->niters < 0 || O->nbetas < 1) {
     snprintf(err, errlen, "oracle: bad nchains/niters/betas");
     return TSA_ERR_ARG;
   }
-  const Par P = make_par(I, O);
+  Par P = make_par(I, O);
   const Models Mo = make_models(O->gpu_model, O->h100_model);
   const int nch = O->nchains, nint = P.nint, nw = I.nw;
   std::vector<float> betas(O->betas, O->betas + O->nbetas);
   if (O->max_levels > 0 && (int)betas.size() > O->max_levels) betas.resize(O->max_levels);
+  // level schedule (treesa_gpu.cu:1758-1764): stage 2 continues the population in mode2
+  std::vector<int> lmode(betas.size(), O->mode), lniters(betas.size(), O->niters);
+  if (O->betas2 && O->nbetas2 > 0)
+    for (int k = 0; k < O->nbetas2; k++) {
+      betas.push_back(O->betas2[k]);
+      lmode.push_back(O->mode2);
+      lniters.push_back(O->niters2 > 0 ? O->niters2 : O->niters);
+    }
+  int mode = O->mode;
   std::vector<uint64_t> S0(nw, 0);
   for (int k = 0; k < O->ninit_slices; k++) {
     int l = O->init_slices[k];
@@ -743,17 +806,18 @@ int orc_run(const tsa_instance* inst, const tsa_options* O, tsa_result* res, cha
   }
   double t_init = now_s() - t_start;
   double t0 = now_s();
+  auto energyE = [&](float lc, int sc, int ns) -> double {  // treesa_gpu.cu:1750-1753
+    return (double)ns + (double)lc + O->sc_weight * std::max(0.0, (double)sc - O->sc_target);
+  };
   auto score = [&](float lc, int sc, int ns) -> double {  // treesa_gpu.cu:1737-1747
     if (O->slicing) return (double)ns + (double)lc + 1000.0 * std::max(0.0, (double)sc - O->sc_target);
     if (O->select_sc) return 4096.0 * std::max(0.0, (double)sc - O->sc_target) + (double)lc;
+    if (mode != 0) return energyE(lc, sc, ns);
     double tc = (double)lc;
     if ((double)sc <= O->sc_target || O->sc_weight <= 0) return tc;
     double pen = log2(O->sc_weight) + (double)sc + log2(1.0 - exp2(O->sc_target - (double)sc));
     double mx = std::max(tc, pen), mn = std::min(tc, pen);
     return mx + log2(1.0 + exp2(mn - mx));
-  };
-  auto energyE = [&](float lc, int sc, int ns) -> double {  // treesa_gpu.cu:1750-1753
-    return (double)ns + (double)lc + O->sc_weight * std::max(0.0, (double)sc - O->sc_target);
   };
   double best_score = INFINITY;
   int best_chain = -1;
@@ -770,12 +834,20 @@ int orc_run(const tsa_instance* inst, const tsa_options* O, tsa_result* res, cha
   std::vector<int> sc(nch), ns(nch);
   const int ee = std::max(1, O->eval_every);
   for (size_t lev = 0; lev < betas.size(); lev++) {
+    if (lmode[lev] != mode) {  // stage switch (treesa_gpu.cu:1793-1799): the incumbent rescored in the new energy
+      HostE H1 = host_energy(I, Mo, best.lab.data(), best.ch.data(), O->slicing ? best.S.data() : nullptr);
+      mode = lmode[lev];
+      P.mode = mode;
+      best_score = score((float)log2(mode == 1 ? H1.time : H1.time2), H1.sc, H1.ns);
+      beta_last = betas[lev];
+    }
     const float beta = betas[lev];
     const uint32_t sw0 = sweep_ctr;
+    const int nit = lniters[lev];
 #pragma omp parallel for schedule(dynamic, 1) reduction(+ : tot_np, tot_na, tot_nsp, tot_nsa, tot_ph)
     for (int c = 0; c < nch; c++) {
       long long np = 0, na = 0, nsp = 0, nsa = 0, ph = 0;
-      for (int it = 0; it < O->niters; it++) {
+      for (int it = 0; it < nit; it++) {
         uint32_t sw = sw0 + (uint32_t)it;
         if (O->order == TSA_ORDER_PAR) par_sweep(I, P, pop[c], beta, sw, (uint32_t)c, np, na, &ph);
         else preorder_sweep(I, P, pop[c], beta, sw, (uint32_t)c, np, na);
@@ -784,9 +856,10 @@ int orc_run(const tsa_instance* inst, const tsa_options* O, tsa_result* res, cha
       }
       tot_np += np, tot_na += na, tot_nsp += nsp, tot_nsa += nsa, tot_ph += ph;
     }
-    sweep_ctr += (uint32_t)O->niters;
+    sweep_ctr += (uint32_t)nit;
     bool last = lev + 1 == betas.size();
-    if ((int)(lev % ee) == ee - 1 || last) {
+    bool switching = !last && lmode[lev + 1] != mode;  // no population step across an energy change
+    if ((int)(lev % ee) == ee - 1 || last || switching) {
 #pragma omp parallel for schedule(dynamic, 4)
       for (int c = 0; c < nch; c++) {
         Eval e = eval_chain(I, P, pop[c]);
@@ -812,10 +885,10 @@ int orc_run(const tsa_instance* inst, const tsa_options* O, tsa_result* res, cha
       for (int c = 0; c < nch; c++)
         if (nfam[family[c]]++ == 0) nf++;
       double row[10] = {now_s() - t0, (double)lev, (double)betas[lev], (double)lc[bi], (double)sc[bi], meanE,
-                        (double)nf, 0.0, (double)ns[bi], meanNs};
+                        (double)nf, (double)mode, (double)ns[bi], meanNs};
       trace.insert(trace.end(), row, row + 10);
       std::vector<int> anc;
-      if (!last && O->scheme == TSA_SCHEME_PA) {  // treesa_gpu.cu:1837-1856
+      if (!last && !switching && O->scheme == TSA_SCHEME_PA) {  // treesa_gpu.cu:1837-1856
         double db = betas[lev + 1] - beta_last;
         beta_last = betas[lev + 1];
         std::vector<double> w(nch);
@@ -834,7 +907,7 @@ int orc_run(const tsa_instance* inst, const tsa_options* O, tsa_result* res, cha
           while (j < nch && j + u < acc) anc[j++] = c;
         }
         while (j < nch) anc[j++] = nch - 1;
-      } else if (!last && O->scheme == TSA_SCHEME_TRUNC) {  // treesa_gpu.cu:1857-1869
+      } else if (!last && !switching && O->scheme == TSA_SCHEME_TRUNC) {  // treesa_gpu.cu:1857-1869
         std::vector<int> idx(nch);
         std::iota(idx.begin(), idx.end(), 0);
         std::sort(idx.begin(), idx.end(),
@@ -927,7 +1000,8 @@ void orc_result_free(tsa_result* r) {
 // start from trees_in (and slice sets S_in, [nch][nw] u64, or NULL) and run nbetas levels of niters
 // sweeps with sweep id lev*niters+it; fixed slice sets (no slice moves).  Writes the final trees and
 // labels.  counters: [0] proposals, [1] accepts, [2] phases.
-int orc_sweeps(const tsa_instance* inst, int order, int par_band, int par_follow, uint64_t seed, double sc_target,
+int orc_sweeps(const tsa_instance* inst, int order, int par_band, int par_follow, int mode, uint64_t seed,
+               double sc_target,
                double sc_weight, const float* betas, int nbetas, int niters, int nch, int c0,
                const uint32_t* trees_in, const uint64_t* S_in, uint32_t* trees_out, uint64_t* labels_out,
                long long* counters, char* err, size_t errlen) {
@@ -936,6 +1010,7 @@ int orc_sweeps(const tsa_instance* inst, int order, int par_band, int par_follow
   tsa_options O{};
   O.par_band = par_band;
   O.par_follow = par_follow;
+  O.mode = mode;
   O.sc_target = sc_target;
   O.sc_weight = sc_weight;
   O.seed = seed;

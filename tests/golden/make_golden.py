@@ -17,7 +17,9 @@ Writes
                      (c) the sq32/sq48 row-major-start results of the reference's large-network
                      benchmark log (bench/results/large_compare_gpu_par.jsonl), par order;
                      (d) as (b) in par order with the CLI's --par-band L and --par-follow variants
-                     (csrc/cpu_ref.h:140-175).
+                     (csrc/cpu_ref.h:140-175);
+                     (e) as (b) with the energy modes gpu and h100 (ref_*<1>, ref_*<2>, default model
+                     constants), both orders.
 """
 import hashlib
 import json
@@ -120,6 +122,19 @@ def main(ref):
                                  niters=4, seed=7, sc_target=24.0, nchains=8, proposals=int(cnt[0]),
                                  accepts=int(cnt[1]), sha256=digest(t, l)))
 
+    # (e) energy modes gpu / h100
+    modes = []
+    for name in ("sat60", "reg3_250", "lat14", "grid24"):
+        rec = inst[name]
+        net = O.Net(rec["ixs"], rec["iy"], rec["nlab"])
+        trees = np.stack([tree_words(rec["tree"])] * 4 + [O.random_tree(net.m, 7, c) for c in range(4, 8)])
+        for mode in ("gpu", "h100"):
+            for order in ("par", "preorder"):
+                t, l, cnt, _ = O.ref_sweeps(net, trees, betas, 4, order=order, seed=7, sc_target=24.0, mode=mode)
+                modes.append(dict(instance=name, order=order, mode=mode, betas=[0.2, 0.7, 7.0], niters=4, seed=7,
+                                  sc_target=24.0, nchains=8, proposals=int(cnt[0]), accepts=int(cnt[1]),
+                                  sha256=digest(t, l)))
+
     # (c) sq32 / sq48 from the row-major path tree (tc / sc identical on RTX 6000 and H100)
     large = []
     for line in open(os.path.join(ref, "bench", "results", "large_compare_gpu_par.jsonl")):
@@ -128,9 +143,9 @@ def main(ref):
             large.append(dict(instance=r["instance"], nchains=r["nchains"], niters=r["niters"], beta0=r["beta0"],
                               tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
     with open(os.path.join(HERE, "expected.json"), "w") as f:
-        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants), f, indent=1)
+        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes), f, indent=1)
     print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}, "
-          f"variants {len(variants)}")
+          f"variants {len(variants)}, modes {len(modes)}")
 
 
 if __name__ == "__main__":

@@ -67,6 +67,16 @@ def test_oracle_matches_cpu_ref_par_variants(golden):
         assert cnt[0] == e["proposals"] and cnt[1] == e["accepts"], e
 
 
+def test_oracle_matches_cpu_ref_energy_modes(golden):
+    """--mode gpu / h100 (cpu_ref.h:42-80, common.h:128-162): the reference's own digests."""
+    for e in golden[1]["modes"]:
+        rec, net = _onet(e["instance"])
+        trees = _util.start_trees(rec, 8, seed=7)
+        t, lab, cnt = O.sweeps(net, trees, CHECK_BETAS, 4, order=e["order"], seed=7, sc_target=24.0, mode=e["mode"])
+        assert _util.digest(t, lab) == e["sha256"], e
+        assert cnt[0] == e["proposals"] and cnt[1] == e["accepts"], e
+
+
 @pytest.mark.skipif(not os.path.exists(O.CPUREF_SO), reason="reference harness not built (no reference sources)")
 @pytest.mark.parametrize("band,follow", [(3, True), (8, False), (0, True)])
 def test_oracle_matches_cpu_ref_live_variants(band, follow):

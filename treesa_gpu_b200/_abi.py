@@ -39,7 +39,8 @@ class Options(C.Structure):
                 ("device", C.c_int32), ("stream", C.c_void_p), ("rank", C.c_int32), ("world_size", C.c_int32),
                 ("nccl_id", C.c_void_p), ("verbose", C.c_int32), ("max_levels", C.c_int32),
                 ("exp_mode", C.c_int32), ("kernel_hint", C.c_int32), ("par_follow", C.c_int32),
-                ("par_band", C.c_int32), ("reserved", C.c_int32 * 10)]
+                ("par_band", C.c_int32), ("mode2", C.c_int32), ("niters2", C.c_int32),
+                ("betas2", C.POINTER(C.c_float)), ("nbetas2", C.c_int32), ("reserved", C.c_int32 * 7)]
 
 
 class Result(C.Structure):
@@ -99,7 +100,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
                  order="par", seed=1, eval_every=1, slicing=False, slice_moves=1, slice_every=1, max_slices=0,
                  init_slices=(), select_sc=False, init_trees=None, gpu_model=None, h100_model=None, device=0,
                  stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc",
-                 exp_mode="host", kernel_hint=0, par_follow=False, par_band=0):
+                 exp_mode="host", kernel_hint=0, par_follow=False, par_band=0, betas2=None, niters2=0, mode2="gpu"):
     o = Options()
     o.betas, _ = keep.arr(np.asarray(betas, np.float32), np.float32, C.c_float)
     o.nbetas = len(betas)
@@ -144,6 +145,11 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
                      "cta_pair": 4}[kernel_hint]
     o.par_follow = int(bool(par_follow))
     o.par_band = int(par_band)
+    if betas2 is not None and len(betas2):
+        o.betas2, _ = keep.arr(np.asarray(betas2, np.float32), np.float32, C.c_float)
+        o.nbetas2 = len(betas2)
+        o.niters2 = int(niters2 or 0)
+        o.mode2 = MODE[mode2]
     return o
 
 
