@@ -59,7 +59,7 @@ typedef struct tsa_options {
   int32_t nbetas;
   int32_t niters;             /* sweeps per beta level */
   int32_t nchains;            /* chains of this call (this rank's shard when world_size > 1) */
-  int32_t mode;               /* TSA_MODE_TC (energy modes 1/2 are not built: TSA_ERR_UNSUPPORTED) */
+  int32_t mode;               /* --mode: TSA_MODE_TC, TSA_MODE_GPU or TSA_MODE_H100 (csrc/common.h:128-222) */
   double sc_target, sc_weight;
   int32_t scheme;             /* TSA_SCHEME_* */
   double trunc_frac;

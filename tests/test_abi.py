@@ -49,7 +49,8 @@ def test_argument_errors_are_reported_not_fatal():
     assert _create([[0, 0], [0, 1], [1]])[0] == 1  # repeated label in a tensor
     assert _create(tri, nlab=2)[0] == 1  # label out of range
     assert _create(tri, iy=[5], nlab=3)[0] == 1  # open label out of range
-    assert _create(tri, mode="gpu")[0] == 4
+    rc, msg = _create(tri, betas2=[1.0, 2.0], mode2="tc")  # stage 2 runs a model energy
+    assert rc == 1 and "stage-2" in msg
     assert _create(tri, betas=[])[0] == 1
     assert _create(tri, nchains=0)[0] == 1
     rc, msg = _create(tri, init_slices=[7])
@@ -63,8 +64,8 @@ def test_argument_errors_are_reported_not_fatal():
 
 def test_run_reports_errors_through_the_python_api():
     import treesa_gpu_b200 as t
-    with pytest.raises(NotImplementedError):
-        t.optimize([[0, 1], [1, 2], [2, 0]], [], mode="gpu")
+    with pytest.raises(ValueError):
+        t.optimize([[0, 1], [1, 2], [2, 0]], [], mode="bogus")
     with pytest.raises(ValueError):
         t.optimize([[0, 1], [1, 2], [2, 0]], [], select="bogus")
     with pytest.raises(TypeError):

@@ -420,6 +420,10 @@ struct tsa_session {
   std::vector<float> betas;
   int niters = 0, nchains = 0, scheme = 0, order = 0, eval_every = 1, slicing = 0, slice_moves = 0;
   int par_band = 0, par_follow = 0;  // par-order variants (--par-band, --par-follow)
+  // energy of every level (stage 2 appends its levels: --stage2-betas/-niters/-mode, :1758-1764)
+  std::vector<int> lmode, lniters;
+  int mode0 = 0;     // energy of the first level
+  int cur_mode = 0;  // energy of the current level (score() depends on it)
   int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1, exp_device = 0;
   double sc_target = 20, sc_weight = 1, trunc_frac = 0.25;
   uint64_t seed = 1;
@@ -498,6 +502,7 @@ struct tsa_session {
   double score(float l, int s, int n) const {  // :1737-1747
     if (slicing) return (double)n + (double)l + 1000.0 * std::max(0.0, (double)s - sc_target);
     if (select_sc) return 4096.0 * std::max(0.0, (double)s - sc_target) + (double)l;
+    if (cur_mode != 0) return energyE(l, s, n);  // the model modes: the log-domain energy
     double tc = (double)l;
     if ((double)s <= sc_target || sc_weight <= 0) return tc;
     double pen = log2(sc_weight) + (double)s + log2(1.0 - exp2(sc_target - (double)s));
@@ -519,8 +524,10 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
     CKR(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     s->own_stream = true;
   }
+  bool model = false;
+  for (int md : s->lmode) model = model || md != TSA_MODE_TC;
   if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, s->order, s->slice_moves, s->par_follow,
-                       &s->plan) !=
+                       model ? 1 : 0, &s->plan) !=
       cudaSuccess) {
     set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
     return TSA_ERR_UNSUPPORTED;
@@ -615,6 +622,7 @@ int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) 
 
 int reset_run_state(tsa_session* s, char* err, size_t errlen) {
   s->ran = false;
+  s->cur_mode = s->mode0;
   s->best_score = INFINITY;
   s->best_chain = s->best_level = -1;
   s->nresample = 0;
@@ -651,10 +659,11 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
     delete s;
     return rc;
   }
-  if (O->mode != TSA_MODE_TC) {
-    set_err(err, errlen, "energy modes gpu/h100 are not built in this version (mode tc only)");
+  if (O->mode < TSA_MODE_TC || O->mode > TSA_MODE_H100 ||
+      (O->betas2 && O->nbetas2 > 0 && O->mode2 != TSA_MODE_GPU && O->mode2 != TSA_MODE_H100)) {
+    set_err(err, errlen, "mode must be tc, gpu or h100, and the stage-2 mode gpu or h100");
     delete s;
-    return TSA_ERR_UNSUPPORTED;
+    return TSA_ERR_ARG;
   }
   if (O->nchains < 1 || O->niters < 0 || O->nbetas < 1 || !O->betas) {
     set_err(err, errlen, "need nchains >= 1, niters >= 0 and at least one beta");
@@ -687,6 +696,15 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   s->betas.assign(O->betas, O->betas + O->nbetas);
   if (O->max_levels > 0 && (int)s->betas.size() > O->max_levels) s->betas.resize(O->max_levels);
   s->niters = O->niters;
+  s->lmode.assign(s->betas.size(), O->mode);
+  s->lniters.assign(s->betas.size(), O->niters);
+  if (O->betas2 && O->nbetas2 > 0)
+    for (int k = 0; k < O->nbetas2; k++) {
+      s->betas.push_back(O->betas2[k]);
+      s->lmode.push_back(O->mode2);
+      s->lniters.push_back(O->niters2 > 0 ? O->niters2 : O->niters);
+    }
+  s->mode0 = s->cur_mode = O->mode;
   s->nchains = O->nchains;
   s->scheme = O->scheme;
   s->order = O->order;
@@ -704,8 +722,10 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   }
   s->par_band = O->order == TSA_ORDER_PAR ? O->par_band : 0;
   s->par_follow = O->order == TSA_ORDER_PAR && O->par_follow ? 1 : 0;
-  if (O->kernel_hint == 3 && (s->par_band || s->par_follow)) {
-    set_err(err, errlen, "kernel_hint 3 (two warps per chain) runs plain par order (no par_band / par_follow)");
+  bool model = false;
+  for (int md : s->lmode) model = model || md != TSA_MODE_TC;
+  if (O->kernel_hint == 3 && (s->par_band || s->par_follow || model)) {
+    set_err(err, errlen, "kernel_hint 3 (two warps per chain) runs plain par order in mode tc");
     delete s;
     return TSA_ERR_ARG;
   }
@@ -812,7 +832,9 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   std::iota(family.begin(), family.end(), 0);
   std::mt19937_64 hrng(splitmix64(s->seed + 777));
   float beta_last = s->betas[0];
-  const bool pipelined = s->scheme == TSA_SCHEME_INDEP && s->plan.kind != tsa::K_BLOCK;
+  bool staged = false;
+  for (int md : s->lmode) staged = staged || md != s->lmode[0];
+  const bool pipelined = s->scheme == TSA_SCHEME_INDEP && s->plan.kind != tsa::K_BLOCK && !staged;
   tsa::SweepArgs a{};
   a.L = s->L;
   a.leaf = s->d_leaf;
@@ -830,6 +852,12 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.slice_moves = s->slice_moves;
   a.par_band = s->par_band;
   a.par_follow = s->par_follow;
+  a.mode = s->cur_mode;
+  {
+    const Models& M = s->models;
+    a.mp = tsa::ModelParams{M.lpeak,    M.lbw,    M.llaunch, M.m0,      M.n0,      M.k0,     M.l3launch, M.lperm2,
+                            M.lcc_bit,  M.lcc_cell, M.ltc_bit, M.ltc_pad, M.ltc_out, M.lsmall_cell, M.small_rank};
+  }
   a.slice_every = s->slice_every;
   a.max_slices = s->max_slices;
   a.stats = s->d_stats;
@@ -864,7 +892,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     for (int c = 0; c < ng; c++)
       if (nfam[family[c]]++ == 0) nf++;
     double row[10] = {now_s() - t0, (double)lev, (double)s->betas[lev], (double)glc[bi], (double)gsc[bi], meanE,
-                      (double)nf, 0.0, (double)gns[bi], meanNs};
+                      (double)nf, (double)s->cur_mode, (double)gns[bi], meanNs};
     s->trace.insert(s->trace.end(), row, row + 10);
     if (s->verbose && (lev % 25 == 0 || lev + 1 == nlev))
       fprintf(stderr, "lev %4zu beta %7.3f  best(l2cost/slice %.3f sc %d |S| %d)  meanE %.3f  families %d  t=%.2fs\n",
@@ -966,6 +994,20 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   } else {
     s->d_cur = s->d_rec;
     for (size_t lev = 0; lev < nlev && rc == TSA_OK; lev++) {
+      if (s->lmode[lev] != s->cur_mode) {
+        // stage switch (:1789-1799): the incumbent, rescored in the new energy, stays the best until beaten
+        s->cur_mode = s->lmode[lev];
+        if (s->best_chain >= 0) {
+          const uint8_t* br = s->h_best;
+          HostE H1 = host_energy(s->I, s->models, reinterpret_cast<const uint64_t*>(br),
+                                 reinterpret_cast<const uint32_t*>(br + s->L.off_ch),
+                                 s->slicing ? reinterpret_cast<const uint64_t*>(br + s->L.off_S) : nullptr);
+          s->best_score = s->score((float)log2(s->cur_mode == TSA_MODE_GPU ? H1.time : H1.time2), H1.sc, H1.ns);
+        }
+        beta_last = s->betas[lev];
+      }
+      a.mode = s->cur_mode;
+      a.nsweeps = s->lniters[lev];
       a.recs = s->d_cur;
       a.recs_out = s->d_cur;
       a.beta = s->betas[lev];
@@ -977,9 +1019,10 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       CKR(tsa::launch_sweeps(a, s->plan, s->st));
       CKR(cudaEventRecord(s->evk[1], s->st));
       s->launches++;
-      s->sweep_ctr += (uint32_t)s->niters;
+      s->sweep_ctr += (uint32_t)s->lniters[lev];
       const bool last = lev + 1 == nlev;
-      const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || last;
+      const bool switching = !last && s->lmode[lev + 1] != s->cur_mode;  // no population step across it
+      const bool eval = (int)(lev % s->eval_every) == s->eval_every - 1 || last || switching;
       if (eval) {
         rc = gather(0, s->st);
         if (rc) break;
@@ -999,7 +1042,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         if ((rc = fetch_best(improved, s->d_cur, s->st))) break;
         CKR(cudaStreamSynchronize(s->st));
       }
-      if (last || s->scheme == TSA_SCHEME_INDEP) continue;
+      if (last || switching || s->scheme == TSA_SCHEME_INDEP) continue;
       std::vector<int> anc(ng);
       if (s->scheme == TSA_SCHEME_PA) {  // :1837-1856
         double db = s->betas[lev + 1] - beta_last;
@@ -1135,7 +1178,7 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
   res->W = 0;
   res->nw = nw;
   res->scheme = s->scheme;
-  res->mode = TSA_MODE_TC;
+  res->mode = s->cur_mode;
   res->nresample = s->nresample;
   res->order = s->order;
   res->ntrace = (int)(s->trace.size() / 10);

@@ -143,6 +143,8 @@ struct WarpCtx {
   float beta, sc_target, sc_weight;
   int slicing;
   int exp_device;
+  int mode;  // energy mode of the launch (the model kernels: 1 gpu, 2 h100)
+  ModelParams mp;
   const float* lse;      // shared
   const double* exptab;  // shared: 2^(j/64)
   const uint64_t* leaf;  // shared
@@ -178,6 +180,67 @@ __device__ __forceinline__ bool accept(const WarpCtx& X_, uint32_t r, float dE) 
   return accept_rt(X_.exp_device, X_.beta, X_.exptab, r, dE);
 }
 
+// float log2(2^a + 2^b) with the device's log2f/exp2f, exactly the reference's lse_f (common.h:121-126)
+__device__ __forceinline__ float lse_f(float a, float b) {
+  float mx = a > b ? a : b;
+  float mn = a > b ? b : a;
+  if (mx == -INFINITY) return mx;
+  return __fadd_rn(mx, log2f(__fadd_rn(1.0f, exp2f(__fsub_rn(mn, mx)))));
+}
+
+struct EvalOut {
+  float lcost;
+  int sc, sc_int, ncand, ns;
+};
+
+// ------------------------------------------------------------------------------------------------
+// Energy modes gpu / h100 (csrc/common.h:128-162): log2 of the modeled time of one pairwise
+// contraction (x, y) -> z with label counts B = |x&y&z|, M = |x&~y&z|, N = |~x&y&z|, K = |x&y&~z|,
+// in the device's float arithmetic (log2f / exp2f through lse_f), as the reference's kernels.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float gpu_lt(int B, int M, int N, int K, const ModelParams& P) {
+  const int Me = M > P.m0 ? M : P.m0, Ne = N > P.n0 ? N : P.n0, Ke = K > P.k0 ? K : P.k0;
+  const float lops = __fsub_rn((float)(1 + B + Me + Ne + Ke), P.lpeak);
+  const float lbits = __fsub_rn(lse_f(lse_f((float)(B + M + K), (float)(B + N + K)), (float)(B + M + N)), P.lbw);
+  return lse_f(lops > lbits ? lops : lbits, P.llaunch);
+}
+__device__ __forceinline__ float h100_lt(int B, int M, int N, int K, const ModelParams& P) {
+  if (B + M + N <= P.small_rank) return __fadd_rn(P.lsmall_cell, (float)(B + M + N + K));
+  const float la = (float)(B + M + K), lb = (float)(B + N + K), lc = (float)(B + M + N);
+  const float lab = lse_f(la, lb), lmoved = lse_f(lab, lc);
+  const float perm = __fadd_rn(P.lperm2, lab);
+  float best = lse_f(__fadd_rn(P.lcc_bit, lmoved), __fadd_rn(P.lcc_cell, (float)(B + M + N + K)));
+  const int MN = M > N ? M : N;
+  if (K >= 7 && MN >= 5) {
+    const int Me = M > 6 ? M : 6, Ne = N > 6 ? N : 6, Ke = K > 8 ? K : 8;
+    const float tc = lse_f(lse_f(__fadd_rn(P.ltc_bit, lmoved), __fadd_rn(P.ltc_pad, (float)(B + Me + Ne + Ke))),
+                           __fadd_rn(P.ltc_out, lc));
+    best = tc < best ? tc : best;
+  }
+  return lse_f(lse_f(P.l3launch, perm), best);
+}
+__device__ __forceinline__ float model_cost(int mode, const ModelParams& P, int B, int M, int N, int K) {
+  return mode == 1 ? gpu_lt(B, M, N, K, P) : h100_lt(B, M, N, K, P);
+}
+// label counts of (x, y) -> z on one masked word (count3, common.h:172-177)
+struct C4 {
+  int B, M, N, K;
+};
+__device__ __forceinline__ void count3(uint64_t x, uint64_t y, uint64_t z, C4& c) {
+  c.B += __popcll(x & y & z);
+  c.M += __popcll(x & ~y & z);
+  c.N += __popcll(~x & y & z);
+  c.K += __popcll(x & y & ~z);
+}
+// dE of a move from the costs of the contractions before (t0) and after (t1) and the sizes
+// (energy_from_counts, common.h:198-222)
+__device__ __forceinline__ float model_energy(float t0, float t1, int sp, int sd, int sx, float sc_target,
+                                              float sc_weight) {
+  const int sc0 = sp > sd ? sp : sd, sc1 = sx > sd ? sx : sd, dsc = sc1 - sc0, scmax = sc0 > sc1 ? sc0 : sc1;
+  const float w = ((float)scmax > sc_target) ? sc_weight : 0.0f;
+  return __fadd_rn(__fmul_rn(w, (float)dsc), __fsub_rn(t1, t0));
+}
+
 // One TreeSA proposal at internal node v (one lane).  Semantics: csrc/cpu_ref.h:89-121 (Julia
 // optimize_subtree! at one node).  With P the pivot child (left for rules 0,1), O the other child,
 // M the pivot's child that moves up and K the one that stays, every rule swaps M and O keeping slots,
@@ -194,7 +257,9 @@ struct Prop {
   int i, Pn, On, Mn, cP1, sx, cV1, sd;
   bool acc;
 };
-template <int NW>
+// MODEL: energy modes gpu / h100; the four contractions (K,M)->P, (P,O)->D, (K,O)->X, (X,M)->D are
+// counted from the label sets as the reference does (cpu_ref.h:69-72), which also needs P's set.
+template <int NW, bool MODEL = false>
 __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* lab, const uint32_t* ch,
                                             const uint32_t* cz, const Set<NW>& NM, int v, uint32_t chv,
                                             uint32_t sweep, uint32_t chain) {
@@ -217,6 +282,7 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
   const uint64_t* pM = p.Mn >= m ? lab + (size_t)(p.Mn - m) * NW : X_.leaf + (size_t)p.Mn * NW;
   Set<NW> D = ldset<NW>(lab + (size_t)p.i * NW), O = ldset<NW>(pO), K = ldset<NW>(pK), M = ldset<NW>(pM);
   int sx = 0, k2 = 0, k3 = 0;
+  C4 c[4] = {};
 #pragma unroll
   for (int w = 0; w < NW; w++) {
     uint64_t x = (K.w[w] | O.w[w]) & (M.w[w] | D.w[w]);
@@ -226,14 +292,33 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
     k2 += __popcll(K.w[w] & O.w[w] & ~x & NM.w[w]);
     k3 += __popcll(xm & M.w[w] & ~D.w[w]);
   }
+  if constexpr (MODEL) {
+    const Set<NW> Pset = ldset<NW>(lab + (size_t)(p.Pn - m) * NW);
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      const uint64_t nm = NM.w[w], k = K.w[w] & nm, mm = M.w[w] & nm, pp = Pset.w[w] & nm, o = O.w[w] & nm,
+                     d = D.w[w] & nm, x = p.X.w[w] & nm;
+      count3(k, mm, pp, c[0]);
+      count3(pp, o, d, c[1]);
+      count3(k, o, x, c[2]);
+      count3(x, mm, d, c[3]);
+    }
+  }
   uint32_t czv = cz[p.i], czp = cz[p.Pn - m];
   p.sd = (int)(czv & 0xFFFFu);
   int sp = (int)(czp & 0xFFFFu);
   p.sx = sx;
   p.cP1 = sx + k2;
   p.cV1 = p.sd + k3;
-  float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, p.sd, sx, p.cP1, p.cV1, X_.sc_target, X_.sc_weight,
-                         X_.lse);
+  float dE;
+  if constexpr (MODEL) {
+    auto cost = [&](const C4& q) { return model_cost(X_.mode, X_.mp, q.B, q.M, q.N, q.K); };
+    dE = model_energy(lse_f(cost(c[0]), cost(c[1])), lse_f(cost(c[2]), cost(c[3])), sp, p.sd, sx, X_.sc_target,
+                      X_.sc_weight);
+  } else {
+    dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, p.sd, sx, p.cP1, p.cV1, X_.sc_target, X_.sc_weight,
+                     X_.lse);
+  }
   p.acc = accept(X_, rnd.y, dE);
   p.nchp = slotM ? ((chp & 0xFFFFu) | ((uint32_t)p.On << 16)) : ((chp & 0xFFFF0000u) | (uint32_t)p.On);
   p.nchv = slotP ? ((chv & 0xFFFF0000u) | (uint32_t)p.Mn) : ((chv & 0xFFFFu) | ((uint32_t)p.Mn << 16));
@@ -253,13 +338,13 @@ __device__ __forceinline__ void apply(const Prop<NW>& p, int m, uint64_t* lab, u
   }
 }
 // propose + apply at one node; returns v's children word after the move (unchanged for a leaf-only node)
-template <int NW, bool PAR, typename C>
+template <int NW, bool PAR, typename C, bool MODEL = false>
 __device__ __forceinline__ uint32_t visit(const WarpCtx& X_, uint64_t* lab, uint32_t* ch, uint32_t* cz,
                                           const Set<NW>& NM, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
                                           C& cnt) {
   const uint32_t chv = ch[v - X_.m];
   if ((int)(chv & 0xFFFFu) < X_.m && (int)(chv >> 16) < X_.m) return chv;
-  Prop<NW> p = propose<NW>(X_, lab, ch, cz, NM, v, chv, sweep, chain);
+  Prop<NW> p = propose<NW, MODEL>(X_, lab, ch, cz, NM, v, chv, sweep, chain);
   cnt.prop++;
   if (p.acc) {
     cnt.acc++;
@@ -278,30 +363,19 @@ __device__ __forceinline__ Set<NW> not_sliced(const uint64_t* S, int slicing) {
   return nm;
 }
 
-// float log2(2^a + 2^b) with the device's log2f/exp2f, exactly the reference's lse_f (common.h:121-126)
-__device__ __forceinline__ float lse_f(float a, float b) {
-  float mx = a > b ? a : b;
-  float mn = a > b ? b : a;
-  if (mx == -INFINITY) return mx;
-  return __fadd_rn(mx, log2f(__fadd_rn(1.0f, exp2f(__fsub_rn(mn, mx)))));
-}
 
-struct EvalOut {
-  float lcost;
-  int sc, sc_int, ncand, ns;
-};
-
-// Whole-chain energy from the (cost, size) cache, in the reference's lane order (eval_chain,
-// csrc/treesa_gpu.cu:386-434): node i accumulated by lane i % 32, then a xor butterfly.
-template <int NW>
-__device__ EvalOut eval_cached(const WarpCtx& X_, const uint32_t* cz, const uint64_t* S, int leaf_sc, int lane) {
+// Whole-chain energy in the reference's lane order (eval_chain, csrc/treesa_gpu.cu:386-434): node i
+// accumulated by lane i % 32, then a xor butterfly.  node(i, Z) returns node i's log2 cost and sets its
+// size Z.
+template <int NW, typename F>
+__device__ EvalOut eval_nodes(const WarpCtx& X_, const uint64_t* S, int leaf_sc, int lane, F&& node) {
   const unsigned FULL = 0xFFFFFFFFu;
   float acc = -INFINITY;
   int scl = 0, cntl = 0;
   for (int i = lane; i < X_.nint; i += 32) {
-    uint32_t w = cz[i];
-    int Z = (int)(w & 0xFFFFu);
-    acc = lse_f(acc, (float)(int)(w >> 16));
+    int Z;
+    const float cost = node(i, Z);
+    acc = lse_f(acc, cost);
     if (Z > scl) {
       scl = Z;
       cntl = 1;
@@ -334,6 +408,43 @@ __device__ EvalOut eval_cached(const WarpCtx& X_, const uint32_t* cz, const uint
     sc = max(scmax, ll);
   }
   return EvalOut{acc, sc, scmax, cnt, ns};
+}
+// tc: from the (cost, size) cache
+template <int NW>
+__device__ EvalOut eval_cached(const WarpCtx& X_, const uint32_t* cz, const uint64_t* S, int leaf_sc, int lane) {
+  return eval_nodes<NW>(X_, S, leaf_sc, lane, [&](int i, int& Z) {
+    const uint32_t w = cz[i];
+    Z = (int)(w & 0xFFFFu);
+    return (float)(int)(w >> 16);
+  });
+}
+// the gpu / h100 models: each node's contraction counted from the label sets (sliced by S)
+template <int NW>
+__device__ EvalOut eval_model(const WarpCtx& X_, const uint64_t* lab, const uint32_t* ch, const uint64_t* S,
+                              int leaf_sc, int lane) {
+  const int m = X_.m;
+  return eval_nodes<NW>(X_, S, leaf_sc, lane, [&](int i, int& Z) {
+    const uint32_t cw = ch[i];
+    const int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+    const Set<NW> x = ldset<NW>(l >= m ? lab + (size_t)(l - m) * NW : X_.leaf + (size_t)l * NW);
+    const Set<NW> y = ldset<NW>(r >= m ? lab + (size_t)(r - m) * NW : X_.leaf + (size_t)r * NW);
+    const Set<NW> z = ldset<NW>(lab + (size_t)i * NW);
+    C4 c{};
+    Z = 0;
+#pragma unroll
+    for (int w = 0; w < NW; w++) {
+      const uint64_t nm = X_.slicing ? ~S[w] : ~0ull, zz = z.w[w] & nm;
+      count3(x.w[w] & nm, y.w[w] & nm, zz, c);
+      Z += __popcll(zz);
+    }
+    return model_cost(X_.mode, X_.mp, c.B, c.M, c.N, c.K);
+  });
+}
+template <int NW, bool MODEL>
+__device__ __forceinline__ EvalOut eval_w(const WarpCtx& X_, const uint64_t* lab, const uint32_t* ch,
+                                          const uint32_t* cz, const uint64_t* S, int leaf_sc, int lane) {
+  if constexpr (MODEL) return eval_model<NW>(X_, lab, ch, S, leaf_sc, lane);
+  else return eval_cached<NW>(X_, cz, S, leaf_sc, lane);
 }
 
 // (cost, size) of every internal node on the network sliced by S (lane-strided), into out[].
@@ -381,10 +492,10 @@ __device__ __forceinline__ int nth_label(const uint64_t* A, const uint64_t* S, i
 
 // Slice moves of one chain (warp-cooperative): slice_step, csrc/treesa_gpu.cu:445-502.  Costs of the
 // proposed slice set are computed into the scratch cache cz2 and committed on accept.
-template <int NW, typename C>
+template <int NW, typename C, bool MODEL = false>
 __device__ void slice_step(const WarpCtx& X_, const SweepArgs& a, uint64_t* lab, uint32_t* ch, uint32_t* cz,
                            uint32_t* cz2, uint64_t* S, uint32_t sweep, uint32_t chain, int lane, C& cnt) {
-  EvalOut cur = eval_cached<NW>(X_, cz, S, a.leaf_sc, lane);
+  EvalOut cur = eval_w<NW, MODEL>(X_, lab, ch, cz, S, a.leaf_sc, lane);
   float Ecur = slice_energy(cur, X_.sc_target, X_.sc_weight);
   for (int j = 0; j < a.slice_moves; j++) {
     U4 r1 = philox10(0x10000u + 2u * j, sweep, chain, 0u, X_.key0, X_.key1);
@@ -422,7 +533,7 @@ __device__ void slice_step(const WarpCtx& X_, const SweepArgs& a, uint64_t* lab,
     __syncwarp();
     recompute_cz<NW>(X_, lab, ch, S, cz2, lane);
     __syncwarp();
-    EvalOut nxt = eval_cached<NW>(X_, cz2, S, a.leaf_sc, lane);
+    EvalOut nxt = eval_w<NW, MODEL>(X_, lab, ch, cz2, S, a.leaf_sc, lane);
     float Enew = slice_energy(nxt, X_.sc_target, X_.sc_weight);
     cnt.sprop++;
     if (accept(X_, r2.x, __fsub_rn(Enew, Ecur))) {
@@ -506,7 +617,7 @@ __device__ __forceinline__ void block_depths(const uint16_t* par, int m, int nin
 // ------------------------------------------------------------------------------------------------
 // k_anneal_warp: nsweeps sweeps of every chain, one warp per chain, chains in shared memory.
 // ------------------------------------------------------------------------------------------------
-template <int NW, int ORDER>
+template <int NW, int ORDER, bool MODEL>
 __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L = a.L;
@@ -538,6 +649,8 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   X_.sc_weight = a.sc_weight;
   X_.slicing = a.slicing;
   X_.exp_device = a.exp_device;
+  X_.mode = a.mode;
+  X_.mp = a.mp;
   X_.lse = s_lse;
   X_.exptab = s_exp;
   X_.leaf = s_leaf;
@@ -677,15 +790,17 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
             key[wl[nint2 - 1 - j]] = 0u;
             cnt.visits++;
           }
-          // more than 32 proposals: two per lane, both evaluated before either is applied
+          // more than 32 proposals: two per lane, both evaluated before either is applied (tc mode and sets
+          // of up to 4 words: above that the two proposals no longer fit in registers)
           int j = lane;
-          for (; nk - (j - lane) > 32; j += 64) {
+          constexpr bool TWO = !MODEL && NW <= 4;
+          for (; TWO && nk - (j - lane) > 32; j += 64) {
             const int ja = j, jb = j + 32;
             const bool vb = jb < nk;
             const int ia = wl[ja], ib = vb ? (int)wl[jb] : ia;
             const uint32_t cha = ch[ia], chb = ch[ib], ka = key[ia], kb = key[ib];
-            Prop<NW> pa = propose<NW>(X_, lab, ch, cz, NM, m + ia, cha, swv(ka), chain);
-            Prop<NW> pb = propose<NW>(X_, lab, ch, cz, NM, m + ib, chb, swv(kb), chain);
+            Prop<NW> pa = propose<NW, MODEL>(X_, lab, ch, cz, NM, m + ia, cha, swv(ka), chain);
+            Prop<NW> pb = propose<NW, MODEL>(X_, lab, ch, cz, NM, m + ib, chb, swv(kb), chain);
             cnt.prop += 1 + vb;
             cnt.acc += pa.acc + (vb && pb.acc);
             cnt.visits += 1 + vb;
@@ -695,21 +810,25 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
             if (vb) key[ib] = 0u;
             if (follow) push(rearm(pa, ka), vb ? rearm(pb, kb) : -1);
           }
-          int ra = -1;
-          if (j < nk) {
-            const int i = wl[j];
-            const uint32_t ki = key[i];
-            Prop<NW> p = propose<NW>(X_, lab, ch, cz, NM, m + i, ch[i], swv(ki), chain);
-            cnt.prop++;
-            cnt.visits++;
-            if (p.acc) {
-              cnt.acc++;
-              apply<NW, true>(p, m, lab, ch, cz, par);
+          // warp-uniform rounds of one proposal per lane (at most one after the paired rounds)
+          for (int b0 = j - lane; b0 < nk; b0 += 32) {
+            const int jj = b0 + lane;
+            int ra = -1;
+            if (jj < nk) {
+              const int i = wl[jj];
+              const uint32_t ki = key[i];
+              Prop<NW> p = propose<NW, MODEL>(X_, lab, ch, cz, NM, m + i, ch[i], swv(ki), chain);
+              cnt.prop++;
+              cnt.visits++;
+              if (p.acc) {
+                cnt.acc++;
+                apply<NW, true>(p, m, lab, ch, cz, par);
+              }
+              key[i] = 0u;
+              ra = rearm(p, ki);
             }
-            key[i] = 0u;
-            ra = rearm(p, ki);
+            if (follow) push(ra, -1);
           }
-          if (follow) push(ra, -1);
           cnt.busy += nk;
           __syncwarp();
         }
@@ -723,7 +842,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
           int v = lane < k ? m + (int)wl[b0 + lane] : 0;
           __syncwarp();
           uint32_t cw = 0;
-          if (lane < k) cw = visit<NW, false>(X_, lab, ch, cz, NM, par, v, sw, chain, cnt);
+          if (lane < k) cw = visit<NW, false, ChainCounters, MODEL>(X_, lab, ch, cz, NM, par, v, sw, chain, cnt);
           // internal children with two leaf children are visited here and now (an empty visit)
           bool c1 = lane < k && (int)(cw & 0xFFFFu) >= m;
           bool c2 = lane < k && (int)(cw >> 16) >= m;
@@ -754,14 +873,14 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
       }
       if (a.slice_moves > 0 && (sw + 1) % (uint32_t)a.slice_every == 0) {
         __syncwarp();
-        slice_step<NW>(X_, a, lab, ch, cz, cz2, S, sw, chain, lane, cnt);
+        slice_step<NW, ChainCounters, MODEL>(X_, a, lab, ch, cz, cz2, S, sw, chain, lane, cnt);
         NM = not_sliced<NW>(S, X_.slicing);
       }
       __syncwarp();
     }
     cnt.flush(tot);
     // ---- energy of the chain after this launch (fused k_energy) ----
-    EvalOut e = eval_cached<NW>(X_, cz, S, a.leaf_sc, lane);
+    EvalOut e = eval_w<NW, MODEL>(X_, lab, ch, cz, S, a.leaf_sc, lane);
     if (lane == 0) {
       a.out_lc[c] = e.lcost;
       a.out_sc[c] = e.sc;
@@ -856,6 +975,8 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
   X_.sc_weight = a.sc_weight;
   X_.slicing = a.slicing;
   X_.exp_device = a.exp_device;
+  X_.mode = a.mode;
+  X_.mp = a.mp;
   X_.lse = s_lse;
   X_.exptab = s_exp;
   X_.leaf = s_leaf;
@@ -1109,6 +1230,8 @@ struct BlkCtx {
   uint32_t key0, key1;
   float beta, sc_target, sc_weight;
   int slicing, exp_device;
+  int mode;  // energy mode of the launch (the model kernels: 1 gpu, 2 h100)
+  ModelParams mp;
   const float* lse;          // shared
   const double* exptab;      // shared
   const uint64_t* leaf;      // global [m][nw]
@@ -1181,7 +1304,7 @@ __device__ __forceinline__ void follow_rearm(const FollowCtx* f, int Pn, int m) 
 }
 
 // sweep: the Philox sweep counter of this visit; fol: re-arm on accept (a first visit with par_follow)
-template <bool SUMS, bool PAR>
+template <bool SUMS, bool PAR, bool MODEL = false>
 __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
                                            int G, int t, unsigned gm, Counters& cnt,
                                            const FollowCtx* fol = nullptr) {
@@ -1209,6 +1332,7 @@ __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v
     u = B.sum[i] | so(On) | so(Kn) | so(Mn);
   }
   int sx = 0, k2 = 0, k3 = 0;
+  C4 cc[4] = {};  // MODEL: (K,M)->P, (P,O)->D, (K,O)->X, (X,M)->D
   for_chunks<SUMS>(u, B.nchunks, G, t, [&](int c) {
     ulonglong2 d = ld2(gD + 2 * c), o = ld2(gO + 2 * c), k = ld2(gK + 2 * c), mm = ld2(gM + 2 * c);
     uint64_t n0 = ~0ull, n1 = ~0ull;
@@ -1221,16 +1345,43 @@ __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v
     sx += __popcll(xm0) + __popcll(xm1);
     k2 += __popcll(k.x & o.x & ~x0 & n0) + __popcll(k.y & o.y & ~x1 & n1);
     k3 += __popcll(xm0 & mm.x & ~d.x) + __popcll(xm1 & mm.y & ~d.y);
+    if constexpr (MODEL) {
+      const ulonglong2 pp = ld2(gP + 2 * c);
+      count3(k.x & n0, mm.x & n0, pp.x & n0, cc[0]);
+      count3(k.y & n1, mm.y & n1, pp.y & n1, cc[0]);
+      count3(pp.x & n0, o.x & n0, d.x & n0, cc[1]);
+      count3(pp.y & n1, o.y & n1, d.y & n1, cc[1]);
+      count3(k.x & n0, o.x & n0, xm0, cc[2]);
+      count3(k.y & n1, o.y & n1, xm1, cc[2]);
+      count3(xm0, mm.x & n0, d.x & n0, cc[3]);
+      count3(xm1, mm.y & n1, d.y & n1, cc[3]);
+    }
   });
   for (int off = G >> 1; off > 0; off >>= 1) {
     sx += __shfl_xor_sync(gm, sx, off);
     k2 += __shfl_xor_sync(gm, k2, off);
     k3 += __shfl_xor_sync(gm, k3, off);
+    if constexpr (MODEL) {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        cc[q].B += __shfl_xor_sync(gm, cc[q].B, off);
+        cc[q].M += __shfl_xor_sync(gm, cc[q].M, off);
+        cc[q].N += __shfl_xor_sync(gm, cc[q].N, off);
+        cc[q].K += __shfl_xor_sync(gm, cc[q].K, off);
+      }
+    }
   }
   uint32_t czv = B.cz[i], czp = B.cz[Pn - m];
   int sd = (int)(czv & 0xFFFFu), sp = (int)(czp & 0xFFFFu);
   int cP1 = sx + k2, cV1 = sd + k3;
-  float dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, B.sc_target, B.sc_weight, B.lse);
+  float dE;
+  if constexpr (MODEL) {
+    auto cost = [&](const C4& q) { return model_cost(B.mode, B.mp, q.B, q.M, q.N, q.K); };
+    dE = model_energy(lse_f(cost(cc[0]), cost(cc[1])), lse_f(cost(cc[2]), cost(cc[3])), sp, sd, sx, B.sc_target,
+                      B.sc_weight);
+  } else {
+    dE = move_energy((int)(czp >> 16), (int)(czv >> 16), sp, sd, sx, cP1, cV1, B.sc_target, B.sc_weight, B.lse);
+  }
   bool acc = accept_rt(B.exp_device, B.beta, B.exptab, rnd.y, dE);
   const int nck = SUMS ? __popcll(u) : B.nchunks;
   if (t == 0) {
@@ -1266,16 +1417,37 @@ __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v
   }
 }
 
+// Model modes: log2 cost of every internal node's contraction, counted from the label sets in HBM on the
+// network sliced by B.S, by all threads of the CTA into costs[] (then read by eval_cz).
+__device__ void block_model_costs(const BlkCtx& B, float* costs) {
+  const int m = B.m, nw = B.nw;
+  for (int i = threadIdx.x; i < B.nint; i += blockDim.x) {
+    const uint32_t cw = B.ch[i];
+    const int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
+    const uint64_t* x = l >= m ? B.lab + (size_t)(l - m) * nw : B.leaf + (size_t)l * nw;
+    const uint64_t* y = r >= m ? B.lab + (size_t)(r - m) * nw : B.leaf + (size_t)r * nw;
+    const uint64_t* z = B.lab + (size_t)i * nw;
+    C4 c{};
+    for (int w = 0; w < nw; w++) {
+      const uint64_t nm = B.slicing ? ~B.S[w] : ~0ull;
+      count3(x[w] & nm, y[w] & nm, z[w] & nm, c);
+    }
+    costs[i] = model_cost(B.mode, B.mp, c.B, c.M, c.N, c.K);
+  }
+  __syncthreads();
+}
+
 // Whole-chain energy from a (cost, size) cache, one warp, in the reference's lane order.
+// costs: the nodes' log2 costs in the model modes (block_model_costs), null for tc (from cz)
 __device__ EvalOut eval_cz(const uint32_t* cz, int nint, const uint64_t* S, int nw, const uint64_t* leaf, int m,
-                           int slicing, int leaf_sc, int lane) {
+                           int slicing, int leaf_sc, int lane, const float* costs = nullptr) {
   const unsigned FULL = 0xFFFFFFFFu;
   float acc = -INFINITY;
   int scl = 0, cntl = 0;
   for (int i = lane; i < nint; i += 32) {
     uint32_t w = cz[i];
     int Z = (int)(w & 0xFFFFu);
-    acc = lse_f(acc, (float)(int)(w >> 16));
+    acc = lse_f(acc, costs ? costs[i] : (float)(int)(w >> 16));
     if (Z > scl) {
       scl = Z;
       cntl = 1;
@@ -1325,13 +1497,15 @@ __device__ __forceinline__ int nth_label_rt(const uint64_t* A, const uint64_t* S
 // Slice moves of one chain, the whole CTA cooperating (slice_step, csrc/treesa_gpu.cu:445-502):
 // warp 0 chooses and judges the proposals; all threads recompute the (cost, size) cache for the
 // proposed slice set.
+// costs: scratch for the model modes' node costs (null in tc mode)
 __device__ void slice_step_block(const BlkCtx& B, const SweepArgs& a, uint32_t* cz2, int* sh, float* shf,
-                                 uint32_t sweep, uint32_t chain, Counters& cnt) {
+                                 uint32_t sweep, uint32_t chain, Counters& cnt, float* costs = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, T = blockDim.x, m = B.m, nw = B.nw;
   EvalOut cur{};
   float Ecur = 0.f;
+  if (costs) block_model_costs(B, costs);
   if (warp == 0) {
-    cur = eval_cz(B.cz, B.nint, B.S, nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+    cur = eval_cz(B.cz, B.nint, B.S, nw, B.leaf, m, B.slicing, a.leaf_sc, lane, costs);
     Ecur = slice_energy(cur, B.sc_target, B.sc_weight);
   }
   for (int j = 0; j < a.slice_moves; j++) {
@@ -1392,8 +1566,9 @@ __device__ void slice_step_block(const BlkCtx& B, const SweepArgs& a, uint32_t* 
       cz2[i] = ((uint32_t)(Z + K) << 16) | (uint32_t)Z;
     }
     __syncthreads();
+    if (costs) block_model_costs(B, costs);  // on the proposed slice set
     if (warp == 0) {
-      EvalOut nxt = eval_cz(cz2, B.nint, B.S, nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+      EvalOut nxt = eval_cz(cz2, B.nint, B.S, nw, B.leaf, m, B.slicing, a.leaf_sc, lane, costs);
       float Enew = slice_energy(nxt, B.sc_target, B.sc_weight);
       U4 r2 = philox10(0x10001u + 2u * j, sweep, chain, 0u, B.key0, B.key1);
       bool acc = accept_rt(B.exp_device, B.beta, B.exptab, r2.x, __fsub_rn(Enew, Ecur));
@@ -1716,7 +1891,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
   }
 }
 
-template <bool SUMS, int ORDER>
+template <bool SUMS, int ORDER, bool MODEL>
 __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L = a.L;
@@ -1742,6 +1917,8 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   B.sc_weight = a.sc_weight;
   B.slicing = a.slicing;
   B.exp_device = a.exp_device;
+  B.mode = a.mode;
+  B.mp = a.mp;
   B.lse = s_lse;
   B.exptab = s_exp;
   B.leaf = a.leaf;
@@ -1756,6 +1933,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   uint16_t* wl = reinterpret_cast<uint16_t*>(smem + Bm.off_wl);
   uint16_t* Ua = reinterpret_cast<uint16_t*>(smem + Bm.off_U);
   uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
+  float* costs = reinterpret_cast<float*>(Ua);  // model modes: node costs, while the U lists are free
   const int m = L.m, nint = L.nint;
   const unsigned lt = (1u << lane) - 1u;
   FlatTabs F;
@@ -1877,7 +2055,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
           // re-armed pivots (par_follow) are appended to U after the nU kept nodes, counted on in sh[1]
           const FollowCtx fctx{pri, U, &sh[1], hs};
           const FollowCtx* fol = follow ? &fctx : nullptr;
-          if constexpr (SUMS) {
+          if constexpr (SUMS && !MODEL) {
             par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{}, fol);
           } else {
             const int G = pick_group(nk, T);
@@ -1886,8 +2064,8 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
             for (int j = g; j < nk; j += groups) {
               int q = wl[j];
               const bool first = (pri[q] & 1u) != 0;  // an even priority marks a follow-up visit
-              visit_coop<SUMS, true>(B, par, m + q, first ? sw : follow_sweep(sw), chain, G, t, gm, cnt,
-                                     first ? fol : nullptr);
+              visit_coop<SUMS, true, MODEL>(B, par, m + q, first ? sw : follow_sweep(sw), chain, G, t, gm, cnt,
+                                            first ? fol : nullptr);
               if (t == 0) {
                 pri[q] = 0;
                 cnt.visits++;
@@ -1922,7 +2100,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
           }
           __syncthreads();
           if (g < k) {
-            visit_coop<SUMS, false>(B, par, m + q, sw, chain, G, t, gm, cnt);
+            visit_coop<SUMS, false, MODEL>(B, par, m + q, sw, chain, G, t, gm, cnt);
             if (t == 0) {
               cnt.visits++;
               uint32_t cw = B.ch[q];
@@ -1941,12 +2119,13 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
       }
       if (a.slice_moves > 0 && (sw + 1) % (uint32_t)a.slice_every == 0) {
         __syncthreads();
-        slice_step_block(B, a, cz2, sh + 8, nullptr, sw, chain, cnt);
+        slice_step_block(B, a, cz2, sh + 8, nullptr, sw, chain, cnt, MODEL ? costs : nullptr);
       }
       __syncthreads();
     }
+    if (MODEL) block_model_costs(B, costs);
     if (warp == 0) {
-      EvalOut e = eval_cz(B.cz, nint, B.S, L.nw, B.leaf, m, B.slicing, a.leaf_sc, lane);
+      EvalOut e = eval_cz(B.cz, nint, B.S, L.nw, B.leaf, m, B.slicing, a.leaf_sc, lane, MODEL ? costs : nullptr);
       if (lane == 0) {
         a.out_lc[c] = e.lcost;
         a.out_sc[c] = e.sc;
@@ -2023,6 +2202,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
   B.sc_weight = a.sc_weight;
   B.slicing = a.slicing;
   B.exp_device = a.exp_device;
+  B.mode = 0;  // tc only (the plan)
   B.lse = s_lse;
   B.exptab = s_exp;
   B.leaf = a.leaf;
@@ -2216,7 +2396,7 @@ __global__ void k_copy(const uint4* __restrict__ src, uint4* __restrict__ dst, c
 // ------------------------------------------------------------------------------------------------
 template <int NW, int ORDER>
 static cudaError_t launch_warp_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
-  auto k = k_anneal_warp<NW, ORDER>;
+  auto k = a.mode != 0 ? k_anneal_warp<NW, ORDER, true> : k_anneal_warp<NW, ORDER, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   if (e != cudaSuccess) return e;
   k<<<p.grid, 32 * p.warps_per_cta, p.smem, st>>>(a, p.warps_per_cta);
@@ -2259,7 +2439,7 @@ static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaSt
 
 template <bool SUMS, int ORDER>
 static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
-  auto k = k_anneal_block<SUMS, ORDER>;
+  auto k = a.mode != 0 ? k_anneal_block<SUMS, ORDER, true> : k_anneal_block<SUMS, ORDER, false>;
   size_t smem = BlockSmem::make(a.L, a.slice_moves).total;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -2306,7 +2486,7 @@ static int cluster_capacity(size_t smem, int grid) {
 }
 
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
-                        int par_follow, LaunchPlan* plan) {
+                        int par_follow, int model, LaunchPlan* plan) {
   int nsm = 0, optin = 0;
   cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
@@ -2362,7 +2542,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   plan->cluster = 1;
   // par order with chunk summaries and at most half as many chains as SMs: a pair of CTAs per chain,
   // if every pair can be resident at once
-  const bool pair_ok = L.sums && order == 0 && slice_moves == 0 && !par_follow;
+  const bool pair_ok = L.sums && order == 0 && slice_moves == 0 && !par_follow && !model;
   if (hint == 4 && !pair_ok) return cudaErrorNotSupported;
   if (pair_ok && (hint == 4 || (hint == 0 && 2 * nchains <= nsm))) {
     const int grid = 2 * nchains;

@@ -24,6 +24,15 @@ struct Layout {
 };
 
 // Everything one sweep launch needs (passed by value).
+// Log-domain constants of the gpu / h100 time models (Params fields of csrc/common.h:80-93, set from
+// the model dictionaries as csrc/treesa_gpu.cu:1460-1475 does).
+struct ModelParams {
+  float lpeak, lbw, llaunch;
+  int m0, n0, k0;
+  float l3launch, lperm2, lcc_bit, lcc_cell, ltc_bit, ltc_pad, ltc_out, lsmall_cell;
+  int small_rank;
+};
+
 struct SweepArgs {
   Layout L;
   uint8_t* recs;             // [nchains] records of rec_bytes (input)
@@ -48,6 +57,8 @@ struct SweepArgs {
   const uint64_t* leaf_sum;  // [m] chunk summaries of the leaf sets (when L.sums)
   int par_band;              // par order: 0, or L = 2..16 (priorities by depth band)
   int par_follow;            // par order: re-visit the pivot child of an accepted first visit
+  int mode;                  // energy of this launch: 0 tc, 1 gpu model, 2 h100 model
+  ModelParams mp;
 };
 
 // Kernel family chosen by the host for a layout.
@@ -64,8 +75,9 @@ struct LaunchPlan {
 // Host-side entry points (tsa_kernels.cu).
 // hint: 0 auto, 1 one warp per chain, 2 one CTA per chain (label sets in HBM), 3 two warps per chain,
 // 4 a pair of CTAs per chain (par order with chunk summaries, no slice moves)
+// model: some level of the run uses an energy mode other than tc
 cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
-                        int par_follow, LaunchPlan* plan);
+                        int par_follow, int model, LaunchPlan* plan);
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
                                cudaStream_t st);

@@ -218,8 +218,6 @@ def optimize(ixs, iy, nchains=1024, betas=None, niters=50, sc_target=20.0, sc_we
     mode = MODE_ALIASES.get(mode, mode)
     if mode not in ("tc", "gpu", "h100", "tc+gpu", "tc+h100"):
         raise ValueError(f"unknown mode {mode!r}")
-    if mode != "tc":
-        raise NotImplementedError(f"energy mode {mode!r} is not built in treesa_gpu_b200 (mode 'tc' only)")
     if select not in ("score", "sc"):
         raise ValueError(f"select must be 'score' or 'sc', got {select!r}")
     if scheme not in ("indep", "pa", "trunc"):
@@ -269,7 +267,11 @@ def optimize(ixs, iy, nchains=1024, betas=None, niters=50, sc_target=20.0, sc_we
                 init_trees=init_trees, gpu_model=[float(gm[k]) for k in GPU_KEYS],
                 h100_model=[float(h100m[k]) for k in H100_KEYS], device=0 if device is None else int(device),
                 verbose=verbose, rank=rank, world_size=world, nccl_id=nccl_id, stream=stream,
-                par_follow=bool(par_follow), par_band=int(par_band or 0))
+                par_follow=bool(par_follow), par_band=int(par_band or 0),
+                mode=mode if mode in ("tc", "gpu", "h100") else "tc")
+    if mode in ("tc+gpu", "tc+h100"):  # stage 2 continues the population in the model energy (driver.py:245-251)
+        opts.update(betas2=_betas32(stage2_betas if stage2_betas is not None else julia_betas(1.0, 0.05, 16.0)),
+                    niters2=int(stage2_niters or niters), mode2=mode.split("+")[1])
     t0 = time.time()
     rc, res = engine.run(net, **opts)
     wall = time.time() - t0
