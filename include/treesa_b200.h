@@ -179,6 +179,17 @@ int tsa_resample(void* records, const int32_t* anc, int32_t nchains, uint32_t re
 int tsa_resample_noalloc(void* records, const int32_t* anc, int32_t nchains, uint32_t rec_bytes, void* stream,
                          char* err, size_t errlen);
 
+/* Spectral start trees (the reference's treesa_gpu/spectral.py: laplacian_vectors, path_cost).
+ * tsa_laplacian_vectors: eigenvectors 2..k+1 (ascending eigenvalues) of the Laplacian of the weighted graph
+ * with n vertices and the nnz unordered pairs (rows[e], cols[e], w[e]) (each pair once), as V[n][k]; dense,
+ * by cuSOLVER's syevdx on the device (loaded at run time).  Replaces laplacian_vectors (spectral.py).
+ * tsa_path_costs: (tc, sc) in log2 of the left-deep path tree contracting the tensors in each of the
+ * norders orderings (orders[norders][m], permutations of 0..m-1).  Replaces path_cost (spectral.py). */
+int tsa_laplacian_vectors(int32_t n, int32_t nnz, const int32_t* rows, const int32_t* cols, const double* w,
+                          int32_t k, int32_t device, double* V, char* err, size_t errlen);
+int tsa_path_costs(const tsa_instance* inst, int32_t norders, const int32_t* orders, int32_t device, double* tc,
+                   int32_t* sc, char* err, size_t errlen);
+
 /* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
  * kernel (1 warp per chain, 2 CTA per chain, 3 two warps per chain, 4 two CTAs per chain), warps per CTA,
  * grid, dynamic shared memory bytes}. */

@@ -213,6 +213,11 @@ def lib():
                                C.c_size_t]
     L.tsa_resample_noalloc.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int32, C.c_uint32, C.c_void_p,
                                        C.c_char_p, C.c_size_t]
+    L.tsa_laplacian_vectors.argtypes = [C.c_int32, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                        C.POINTER(C.c_double), C.c_int32, C.c_int32, C.POINTER(C.c_double),
+                                        C.c_char_p, C.c_size_t]
+    L.tsa_path_costs.argtypes = [C.POINTER(Instance), C.c_int32, C.POINTER(C.c_int32), C.c_int32,
+                                 C.POINTER(C.c_double), C.POINTER(C.c_int32), C.c_char_p, C.c_size_t]
     v = L.tsa_abi_version()
     if v != ABI_VERSION:
         raise RuntimeError(f"libtreesa_b200.so ABI version {v}, expected {ABI_VERSION}")

@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 GEN = os.path.join(CSRC, "gen")
 LIB = os.path.join(HERE, "libtreesa_b200.so")
 ROOT = os.path.dirname(HERE)
-SOURCES = ["tsa_kernels.cu", "tsa_host.cpp", "tsa_comm.cpp", "tsa_resample_noalloc.cu"]
+SOURCES = ["tsa_kernels.cu", "tsa_host.cpp", "tsa_comm.cpp", "tsa_resample_noalloc.cu", "tsa_spectral.cu"]
 HEADERS = ["tsa_core.h", "tsa_exp_table.h", "tsa_kernels.cuh", "tsa_comm.h"]
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 

@@ -249,7 +249,7 @@ def optimize(ixs, iy, nchains=1024, betas=None, niters=50, sc_target=20.0, sc_we
             d0s = [greedy_tree(ixs, iy)]
         elif init == "spectral":
             from . import spectral as _sp
-            so = _sp.spectral_orders(ixs, iy, k=spectral_k, seed=seed)
+            so = _sp.spectral_orders(ixs, iy, k=spectral_k, seed=seed, device=0 if device is None else int(device))
             d0s = [_sp.path_tree(o) for _, _, o in so]
             spectral_tcs = [round(t, 4) for t, _, _ in so]
         else:

@@ -147,3 +147,34 @@ def nccl_unique_id():
     rc = _abi.lib().tsa_nccl_unique_id(buf, err, 512)
     _abi.check(rc, err, "tsa_nccl_unique_id")
     return buf.raw
+
+
+def laplacian_vectors(n, rows, cols, w, k=3, device=0):
+    """Eigenvectors 2..k+1 of the weighted graph Laplacian on the GPU (tsa_laplacian_vectors, cuSOLVER)."""
+    L = _abi.lib()
+    r = np.ascontiguousarray(rows, np.int32)
+    c = np.ascontiguousarray(cols, np.int32)
+    ww = np.ascontiguousarray(w, np.float64)
+    V = np.zeros((n, k), np.float64)
+    err = C.create_string_buffer(512)
+    p = lambda x, t: x.ctypes.data_as(C.POINTER(t))  # noqa: E731
+    rc = L.tsa_laplacian_vectors(int(n), len(ww), p(r, C.c_int32), p(c, C.c_int32), p(ww, C.c_double), int(k),
+                                 int(device), p(V, C.c_double), err, 512)
+    _abi.check(rc, err, "tsa_laplacian_vectors")
+    return V
+
+
+def path_costs(net, orders, device=0):
+    """(tc, sc) arrays of the path trees of a batch of tensor orderings on the GPU (tsa_path_costs)."""
+    L = _abi.lib()
+    o = np.ascontiguousarray(orders, np.int32)
+    if o.ndim == 1:
+        o = o[None, :]
+    tc = np.zeros(o.shape[0], np.float64)
+    sc = np.zeros(o.shape[0], np.int32)
+    err = C.create_string_buffer(512)
+    rc = L.tsa_path_costs(C.byref(net.inst), o.shape[0], o.ctypes.data_as(C.POINTER(C.c_int32)), int(device),
+                          tc.ctypes.data_as(C.POINTER(C.c_double)), sc.ctypes.data_as(C.POINTER(C.c_int32)), err, 512)
+    _abi.check(rc, err, "tsa_path_costs")
+    return tc, sc
+

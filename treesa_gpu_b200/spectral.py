@@ -15,6 +15,10 @@ treesa_gpu/spectral.py (tensor_graph, laplacian_vectors, path_cost, path_tree, s
   orderings are returned so that different chains can start from different trees.
 
 The orderings depend on the eigensolver, so they are compared on tc, not as exact permutations.
+
+With a ``device``, both numerical parts run on that GPU through libtreesa_b200.so: the eigenvectors by
+cuSOLVER on the dense Laplacian (tsa_laplacian_vectors) and every batch of candidate orderings scored by
+one kernel launch (tsa_path_costs); the search itself is the same.
 """
 import math
 
@@ -44,9 +48,12 @@ def tensor_graph(ixs):
     return n, keys[:, 0], keys[:, 1], np.array(list(acc.values()), np.float64)
 
 
-def laplacian_vectors(n, rows, cols, w, k=3, dense_max=3000, seed=0):
+def laplacian_vectors(n, rows, cols, w, k=3, dense_max=3000, seed=0, device=None):
     """Eigenvectors 1..k (the lowest skipped) of the graph Laplacian, as the columns of an (n, k) array."""
     k = max(1, min(k, n - 2))
+    if device is not None:
+        from . import engine
+        return engine.laplacian_vectors(n, rows, cols, w, k=k, device=device)
     deg = np.zeros(n)
     np.add.at(deg, rows, w)
     np.add.at(deg, cols, w)
@@ -115,44 +122,71 @@ def path_tree(order):
     return t
 
 
-def spectral_orders(ixs, iy=(), k=8, nangles=24, nrandom=24, seed=0, dense_max=3000):
-    """The ``k`` best distinct spectral orderings: list of (tc, sc, order), best first."""
+def _gpu_scorer(ixs, iy, device):
+    """score(list of orderings) -> list of (tc, sc), one kernel launch per call."""
+    from . import engine
+    lmap = {}
+    for ix in ixs:
+        for l in ix:
+            lmap.setdefault(l, len(lmap))
+    for l in iy:
+        lmap.setdefault(l, len(lmap))
+    net = engine.Network([[lmap[l] for l in ix] for ix in ixs], [lmap[l] for l in iy], max(1, len(lmap)))
+
+    def score(orders):
+        tc, sc = engine.path_costs(net, np.array(orders, np.int32), device=device)
+        return [(float(a), int(b)) for a, b in zip(tc, sc)]
+    return score
+
+
+def spectral_orders(ixs, iy=(), k=8, nangles=24, nrandom=24, seed=0, dense_max=3000, device=None):
+    """The ``k`` best distinct spectral orderings: list of (tc, sc, order), best first.  With a ``device``
+    the eigenvectors and the path costs are computed on that GPU."""
     n = len(ixs)
     if n < 3:
         return [(0.0, 0, list(range(n)))]
     n_, rows, cols, w = tensor_graph(ixs)
-    V = laplacian_vectors(n, rows, cols, w, k=3, dense_max=dense_max, seed=seed)
+    V = laplacian_vectors(n, rows, cols, w, k=3, dense_max=dense_max, seed=seed, device=device)
     d = V.shape[1]
     rng = np.random.default_rng(seed)
     cands, seen = [], set()
+    if device is not None:
+        score = _gpu_scorer(ixs, iy, device)
+    else:
+        def score(orders):
+            return [path_cost(o, ixs, iy) for o in orders]
+
+    def try_dirs(vs):
+        """Candidates of the directions vs (both senses each), scored together; best tc per direction."""
+        todo, owner = [], []
+        for j, v in enumerate(vs):
+            o = np.argsort(V @ v, kind="stable")
+            for oo in (o, o[::-1]):
+                key = oo.tobytes()
+                if key in seen:
+                    continue
+                seen.add(key)
+                todo.append(oo.tolist())
+                owner.append(j)
+        best = [None] * len(vs)
+        for (tc, sc), oo, j in zip(score(todo) if todo else [], todo, owner):
+            cands.append((tc, sc, oo, np.array(vs[j], float)))
+            best[j] = tc if best[j] is None else min(best[j], tc)
+        return best
 
     def try_dir(v):
-        x = V @ v
-        o = np.argsort(x, kind="stable")
-        best = None
-        for oo in (o, o[::-1]):
-            key = oo.tobytes()
-            if key in seen:
-                continue
-            seen.add(key)
-            tc, sc = path_cost(oo.tolist(), ixs, iy)
-            cands.append((tc, sc, oo.tolist(), np.array(v, float)))
-            best = tc if best is None else min(best, tc)
-        return best
+        return try_dirs([v])[0]
 
     def plane(th):
         v = np.zeros(d)
         v[0], v[1] = math.cos(th), math.sin(th)
         return v
 
-    if d >= 2:
-        for a in range(nangles):
-            try_dir(plane(math.pi * a / nangles))
-    else:
-        try_dir(np.ones(1))
+    first = [plane(math.pi * a / nangles) for a in range(nangles)] if d >= 2 else [np.ones(1)]
     for _ in range(nrandom if d >= 3 else 0):
         v = rng.standard_normal(d)
-        try_dir(v / np.linalg.norm(v))
+        first.append(v / np.linalg.norm(v))
+    try_dirs(first)
     if d >= 2:
         # local refinement of the angle around the three best plane directions (a small tilt orders the
         # sites inside a wavefront on lattices)
