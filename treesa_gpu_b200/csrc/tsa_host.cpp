@@ -574,10 +574,9 @@ int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) 
   const Inst& I = s->I;
   const Layout& L = s->L;
   const int nint = L.nint, nw = L.nw, K = O->init_trees ? O->ntrees : 0;
-  std::vector<uint8_t> host((size_t)L.rec_bytes * s->nchains, 0);
   // distinct start trees: K given trees (chain c from tree c % K), else one random tree per chain
   const int ndist = K > 0 ? std::min(K, s->nglobal) : s->nchains;
-  std::vector<std::vector<uint8_t>> recs(K > 0 ? ndist : 0);
+  std::vector<uint8_t> host((size_t)L.rec_bytes * (K > 0 ? ndist : s->nchains), 0);
   int bad = 0;
   auto build = [&](const uint32_t* tree, uint8_t* rec) -> bool {
     uint64_t* lab = reinterpret_cast<uint64_t*>(rec);
@@ -593,13 +592,8 @@ int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) 
   };
   if (K > 0) {
 #pragma omp parallel for schedule(dynamic, 1) reduction(+ : bad)
-    for (int k = 0; k < ndist; k++) {
-      recs[k].assign(L.rec_bytes, 0);
-      if (!build(O->init_trees + (size_t)k * nint, recs[k].data())) bad++;
-    }
-    if (!bad)
-      for (int c = 0; c < s->nchains; c++)
-        memcpy(&host[(size_t)c * L.rec_bytes], recs[(s->chain0 + c) % K].data(), L.rec_bytes);
+    for (int k = 0; k < ndist; k++)
+      if (!build(O->init_trees + (size_t)k * nint, &host[(size_t)k * L.rec_bytes])) bad++;
   } else {
 #pragma omp parallel for schedule(dynamic, 4) reduction(+ : bad)
     for (int c = 0; c < s->nchains; c++) {
@@ -612,9 +606,20 @@ int init_chains(tsa_session* s, const tsa_options* O, char* err, size_t errlen) 
     set_err(err, errlen, "invalid initial tree");
     return TSA_ERR_ARG;
   }
-  const size_t bytes = host.size();
-  CKR(cudaMemcpyAsync(s->d_init, host.data(), bytes, cudaMemcpyHostToDevice, s->st));
-  s->h2d += bytes;
+  const size_t bytes = (size_t)L.rec_bytes * s->nchains;
+  if (K > 0) {
+    // the ndist distinct records go up once and are replicated on the device: chain c <- record
+    // (chain0 + c) % K (staged in d_rec2, which the run overwrites before reading)
+    std::vector<int> src(s->nchains);
+    for (int c = 0; c < s->nchains; c++) src[c] = (s->chain0 + c) % K;
+    CKR(cudaMemcpyAsync(s->d_rec2, host.data(), host.size(), cudaMemcpyHostToDevice, s->st));
+    CKR(cudaMemcpyAsync(s->d_anc, src.data(), sizeof(int) * s->nchains, cudaMemcpyHostToDevice, s->st));
+    s->h2d += host.size() + sizeof(int) * s->nchains;
+    CKR(tsa::launch_copy_chains(s->d_rec2, s->d_init, s->d_anc, s->nchains, L.rec_bytes, s->st));
+  } else {
+    CKR(cudaMemcpyAsync(s->d_init, host.data(), bytes, cudaMemcpyHostToDevice, s->st));
+    s->h2d += bytes;
+  }
   CKR(cudaMemcpyAsync(s->d_rec, s->d_init, bytes, cudaMemcpyDeviceToDevice, s->st));
   CKR(cudaStreamSynchronize(s->st));
   return TSA_OK;
