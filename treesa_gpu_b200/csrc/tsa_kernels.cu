@@ -1634,6 +1634,38 @@ struct Item {
 };
 __device__ __forceinline__ Item item_of(uint32_t it) { return Item{(int)(it >> 16), (int)(it & 0xFFFFu)}; }
 
+// position of the k-th (0-based) set bit of x; k < popc(x)
+__device__ __forceinline__ int nth_bit32(uint32_t x, int k) {
+  int pos = 0;
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1) {
+    const int c = __popc(x & ((1u << w) - 1u));
+    if (k >= c) {
+      k -= c;
+      x >>= w;
+      pos += w;
+    }
+  }
+  return pos;
+}
+// Item e of a batch of nb nodes found without a list: the last node whose first item is <= e (nodes without
+// items share their successor's offset and are never returned for a valid e), its chunk the k-th set bit
+// of its union.  Used when a batch has at most two items per thread, where it saves the list's build and
+// barrier; wider batches read the list (flat_build).
+__device__ __forceinline__ Item flat_decode(const FlatTabs& F, int nb, int e) {
+  int lo = 0, hi = nb - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if ((int)F.off[mid] <= e) lo = mid;
+    else hi = mid - 1;
+  }
+  const int k = e - (int)F.off[lo];
+  const uint64_t u = F.u[lo];
+  const uint32_t ul = (uint32_t)u;
+  const int nl = __popc(ul);
+  return Item{lo, k < nl ? nth_bit32(ul, k) : 32 + nth_bit32((uint32_t)(u >> 32), k - nl)};
+}
+
 // The items numbered [w0, w0 + kFlatItems) into F.items.  A warp whose owners have fewer than 32 chunks
 // each lets every owner write its own items (as many steps as the widest owner has chunks); otherwise
 // the warp expands the masks of its 32 owners together: for owner o, lane l writes the item of chunk l
@@ -1793,17 +1825,22 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     if (tid < nb) F.off[tid] = (uint32_t)(incl - nck + (warp ? F.scan[warp - 1] : 0));
     const int total = F.scan[nwarps - 1];
     __syncthreads();
-    // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first two items
+    // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first two items.  A batch of
+    // at most 2T items decodes each item's node and chunk directly (no list)
     Item k0{-1, 0}, k1{-1, 0};
     ulonglong2 x0 = make_ulonglong2(0ull, 0ull), x1 = x0;
+    const bool direct = total <= 2 * T;
     for (int w0 = 0; w0 < total; w0 += kFlatItems) {
-      if (w0) __syncthreads();  // the previous window's items are consumed
-      flat_build(F, nb, w0);
-      __syncthreads();
+      if (!direct) {
+        if (w0) __syncthreads();  // the previous window's items are consumed
+        flat_build(F, nb, w0);
+        __syncthreads();
+      }
       const int nwin = min(kFlatItems, total - w0);
+      auto item = [&](int e) { return direct ? flat_decode(F, nb, e) : item_of(F.items[e]); };
       int e = tid;
       for (; e + T < nwin; e += 2 * T) {  // two items: all eight loads issued before either is used
-        const Item i0 = item_of(F.items[e]), i1 = item_of(F.items[e + T]);
+        const Item i0 = item(e), i1 = item(e + T);
         const ItemSets s0 = flat_load<CL>(B, F, wlb, i0);
         const ItemSets s1 = flat_load<CL>(B, F, wlb, i1);
         const ItemX r0 = flat_compute(B, i0, s0), r1 = flat_compute(B, i1, s1);
@@ -1818,7 +1855,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
         cnt.busy += 2;
       }
       if (e < nwin) {
-        const Item i0 = item_of(F.items[e]);
+        const Item i0 = item(e);
         const ItemX r0 = flat_eval<CL>(B, F, wlb, i0);
         flat_add(F, i0.j, r0);
         if (w0 == 0 && e == tid) {
