@@ -28,7 +28,8 @@ def main():
                                               scheme=scheme, order=order, init="random", seed=3)
             out[f"{scheme}-{order}"] = dict(tc=info["tc"], sc=info["sc"], best_chain=info["best_chain"],
                                             proposals=info["proposals"], nresample=info["nresample"],
-                                            nchains=info["nchains"], valid=info["valid"])
+                                            nchains=info["nchains"], valid=info["valid"],
+                                            trace=[row[1:] for row in info["trace"]])
     allout = [None] * dist.get_world_size()
     dist.all_gather_object(allout, out)
     if dist.get_rank() == 0:

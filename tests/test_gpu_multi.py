@@ -47,3 +47,11 @@ def test_two_gpu_runs_equal_one_gpu_run(tmp_path):
         assert r["valid"] and r["nchains"] == 2 * n
         assert (r["tc"], r["sc"], r["best_chain"], r["proposals"], r["nresample"]) == \
             (info["tc"], info["sc"], info["best_chain"], info["proposals"], info["nresample"]), key
+        # per-level trace without the time column: the level's best and the families exactly; the means
+        # (summed per rank under best-of-N, then over ranks) to rounding
+        ref = [row[1:] for row in info["trace"]]
+        assert len(r["trace"]) == len(ref), key
+        for a, b in zip(r["trace"], ref):
+            exact = [0, 1, 2, 3, 5, 6, 7]
+            assert [a[i] for i in exact] == [b[i] for i in exact], key
+            assert a[4] == pytest.approx(b[4], rel=1e-12) and a[8] == pytest.approx(b[8], rel=1e-12), key

@@ -91,6 +91,8 @@ struct CommImpl {
   uint8_t* recbuf = nullptr;
   size_t rec_cap = 0;
   unsigned long long* u64buf = nullptr;
+  double* dbuf = nullptr;
+  size_t dcap = 0;
   int* d_idx = nullptr;
   int idx_cap = 0;
 };
@@ -250,6 +252,28 @@ int Comm::sum_u64(uint64_t* host_vals, int n, cudaStream_t st, char* err, size_t
   CCK(cudaMemcpyAsync(p->u64buf, host_vals, n * 8, cudaMemcpyHostToDevice, st));
   NCK(p->N->allReduce(p->u64buf, p->u64buf, n, ncclUint64, ncclSum, p->comm, st));
   CCK(cudaMemcpyAsync(host_vals, p->u64buf, n * 8, cudaMemcpyDeviceToHost, st));
+  CCK(cudaStreamSynchronize(st));
+  return TSA_OK;
+}
+
+int Comm::allgather_host(const double* host_in, int n, double* host_out, cudaStream_t st, char* err,
+                         size_t errlen) {
+  const size_t tot = (size_t)n * (world + 1);  // [own n | gathered world*n]
+  int rc = grow(&p->dbuf, &p->dcap, std::max<size_t>(tot, 1), err, errlen);
+  if (rc) return rc;
+  CCK(cudaMemcpyAsync(p->dbuf, host_in, (size_t)n * sizeof(double), cudaMemcpyHostToDevice, st));
+  NCK(p->N->allGather(p->dbuf, p->dbuf + n, n, ncclFloat64, p->comm, st));
+  CCK(cudaMemcpyAsync(host_out, p->dbuf + n, (size_t)n * world * sizeof(double), cudaMemcpyDeviceToHost, st));
+  CCK(cudaStreamSynchronize(st));
+  return TSA_OK;
+}
+
+int Comm::bcast_host(uint8_t* host, uint32_t bytes, int owner, cudaStream_t st, char* err, size_t errlen) {
+  int rc = grow(&p->recbuf, &p->rec_cap, bytes, err, errlen);
+  if (rc) return rc;
+  if (rank == owner) CCK(cudaMemcpyAsync(p->recbuf, host, bytes, cudaMemcpyHostToDevice, st));
+  NCK(p->N->broadcast(p->recbuf, p->recbuf, bytes, ncclUint8, owner, p->comm, st));
+  if (rank != owner) CCK(cudaMemcpyAsync(host, p->recbuf, bytes, cudaMemcpyDeviceToHost, st));
   CCK(cudaStreamSynchronize(st));
   return TSA_OK;
 }

@@ -1,9 +1,11 @@
 // tsa_comm.h -- multi-GPU layer of libtreesa_b200.so: one process per GPU, chains sharded by rank
 // (rank r owns global chains [r*n, (r+1)*n)).  NCCL (loaded with dlopen, so single-GPU use needs no
 // NCCL) carries the only exchanges the annealer has:
-//   * allgather of every chain's (lcost, sc, |S|) after an evaluated level, so that every rank computes
-//     the same best-of-N choice and the same resampling ancestors;
-//   * broadcast of the best chain's record from its owner when the best improves;
+//   * population schemes: allgather of every chain's (lcost, sc, |S|) after an evaluated level, so that
+//     every rank computes the same resampling ancestors, and broadcast of the best chain's record from
+//     its owner when the best improves;
+//   * best-of-N: every rank scores its own chains level by level; one allgather of the per-level
+//     summaries and of each rank's best at the end, then a broadcast of the winner's record;
 //   * population resampling: chains whose ancestor lives on another rank are sent once per (source,
 //     destination rank) pair with grouped ncclSend/ncclRecv into the receiver's own staging buffer,
 //     then every rank gathers its new population locally.
@@ -29,6 +31,10 @@ struct Comm {
   int resample(const int* anc_global, uint8_t* d_rec, uint8_t* d_rec2, int* d_anc, int nloc, uint32_t rec_bytes,
                cudaStream_t st, char* err, size_t errlen);
   int sum_u64(uint64_t* host_vals, int n, cudaStream_t st, char* err, size_t errlen);
+  // synchronous: n doubles from every rank, in rank order, into host_out[world*n]
+  int allgather_host(const double* host_in, int n, double* host_out, cudaStream_t st, char* err, size_t errlen);
+  // synchronous: the owner's host buffer copied into every rank's host buffer
+  int bcast_host(uint8_t* host, uint32_t bytes, int owner, cudaStream_t st, char* err, size_t errlen);
 };
 
 int comm_create(const void* id128, int rank, int world, int device, Comm** out, char* err, size_t errlen);

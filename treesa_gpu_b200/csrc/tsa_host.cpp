@@ -19,6 +19,7 @@
 #include <numeric>
 #include <random>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/treesa_b200.h"
@@ -903,26 +904,107 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       fprintf(stderr, "lev %4zu beta %7.3f  best(l2cost/slice %.3f sc %d |S| %d)  meanE %.3f  families %d  t=%.2fs\n",
               lev, s->betas[lev], (double)glc[bi], gsc[bi], gns[bi], meanE, nf, now_s() - t0);
   };
-  // enqueue on stream cs: energies of this level (all ranks) into pinned host slot q
+  // Best-of-N over several ranks needs no exchange per level: every rank scores its own chains and keeps
+  // its own best record (process_local), and one exchange after the last level (reduce_local) picks the
+  // global best and rebuilds the trace.  The first strict improvement in (level, chain) order is the
+  // smallest (score, level, chain), so the winner is the chain a single-rank run of the whole population
+  // picks.  Population schemes and staged runs (whose incumbent is rescored at the stage switch) gather
+  // every chain's energies after each evaluated level.
+  const bool local = s->world > 1 && s->scheme == TSA_SCHEME_INDEP && !staged;
+  constexpr int kLS = 9;     // per evaluated level: t, level, best score, its global chain, lc, sc, |S|, sum E, sum |S|
+  std::vector<double> lsum;  // this rank's summaries of the evaluated levels
+  auto process_local = [&](size_t lev, int q, int* improved) {
+    const size_t off = (size_t)q * ng + (size_t)s->rank * nch;
+    const float* lc = s->h_lc + off;
+    const int *sc = s->h_sc + off, *ns = s->h_ns + off;
+    int bi = 0;
+    double bs = INFINITY, sumE = 0, sumNs = 0;
+    for (int c = 0; c < nch; c++) {
+      double sv = s->score(lc[c], sc[c], ns[c]);
+      if (sv < bs) {
+        bs = sv;
+        bi = c;
+      }
+      sumE += s->energyE(lc[c], sc[c], ns[c]);
+      sumNs += ns[c];
+    }
+    const int g = s->rank * nch + bi;
+    *improved = -1;
+    if (bs < s->best_score) {
+      s->best_score = bs;
+      s->best_chain = g;
+      s->best_level = (int)lev;
+      *improved = g;
+    }
+    const double row[kLS] = {now_s() - t0, (double)lev, bs, (double)g, (double)lc[bi], (double)sc[bi],
+                             (double)ns[bi], sumE, sumNs};
+    lsum.insert(lsum.end(), row, row + kLS);
+  };
+  auto reduce_local = [&]() -> int {
+    const int n = 3 + (int)lsum.size();
+    std::vector<double> mine(n), all((size_t)n * s->world);
+    mine[0] = s->best_score;
+    mine[1] = s->best_level;
+    mine[2] = s->best_chain;
+    std::copy(lsum.begin(), lsum.end(), mine.begin() + 3);
+    int rc2 = s->comm->allgather_host(mine.data(), n, all.data(), s->st, err, errlen);
+    if (rc2) return rc2;
+    int owner = -1;
+    for (int r = 0; r < s->world; r++) {
+      const double* m = &all[(size_t)r * n];
+      if (m[2] < 0) continue;
+      const double* o = owner >= 0 ? &all[(size_t)owner * n] : nullptr;
+      if (!o || std::make_tuple(m[0], m[1], m[2]) < std::make_tuple(o[0], o[1], o[2])) owner = r;
+    }
+    if (owner >= 0) {
+      const double* m = &all[(size_t)owner * n];
+      s->best_score = m[0];
+      s->best_level = (int)m[1];
+      s->best_chain = (int)m[2];
+      if ((rc2 = s->comm->bcast_host(s->h_best, rb, owner, s->st, err, errlen))) return rc2;
+      if (s->rank != owner) s->d2h += rb;
+    }
+    const int nev = (int)lsum.size() / kLS;
+    for (int e = 0; e < nev; e++) {
+      auto at = [&](int r) { return &all[(size_t)r * n + 3 + (size_t)e * kLS]; };
+      int br = 0;
+      double sE = 0, sN = 0;
+      for (int r = 0; r < s->world; r++) {
+        if (at(r)[2] < at(br)[2]) br = r;
+        sE += at(r)[7];
+        sN += at(r)[8];
+      }
+      const double* b = at(br);
+      const size_t lev = (size_t)b[1];
+      const double row[10] = {at(0)[0], b[1], (double)s->betas[lev], b[4], b[5], sE / ng, (double)ng,
+                              (double)s->cur_mode, b[6], sN / ng};
+      s->trace.insert(s->trace.end(), row, row + 10);
+      if (s->verbose && (lev % 25 == 0 || lev + 1 == nlev))
+        fprintf(stderr, "lev %4zu beta %7.3f  best(l2cost/slice %.3f sc %d |S| %d)  meanE %.3f  families %d  t=%.2fs\n",
+                lev, s->betas[lev], b[4], (int)b[5], (int)b[6], sE / ng, ng, at(0)[0]);
+    }
+    return TSA_OK;
+  };
+  // enqueue on stream cs: energies of this level into pinned host slot q (every rank's with the gather,
+  // else this rank's, at its place in the slot)
   auto gather = [&](int q, cudaStream_t cs) -> int {
-    if (s->world > 1)
+    if (s->world > 1 && !local)
       return s->comm->allgather_energies(s->d_lc + (size_t)q * nch, s->d_sc + (size_t)q * nch,
                                          s->d_ns + (size_t)q * nch, nch, s->h_lc + (size_t)q * ng,
                                          s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, cs, err, errlen);
-    CKR(cudaMemcpyAsync(s->h_lc + (size_t)q * ng, s->d_lc + (size_t)q * nch, nch * sizeof(float),
-                        cudaMemcpyDeviceToHost, cs));
-    CKR(cudaMemcpyAsync(s->h_sc + (size_t)q * ng, s->d_sc + (size_t)q * nch, nch * sizeof(int),
-                        cudaMemcpyDeviceToHost, cs));
-    CKR(cudaMemcpyAsync(s->h_ns + (size_t)q * ng, s->d_ns + (size_t)q * nch, nch * sizeof(int),
-                        cudaMemcpyDeviceToHost, cs));
+    const size_t off = (size_t)q * ng + (size_t)s->rank * nch;
+    CKR(cudaMemcpyAsync(s->h_lc + off, s->d_lc + (size_t)q * nch, nch * sizeof(float), cudaMemcpyDeviceToHost, cs));
+    CKR(cudaMemcpyAsync(s->h_sc + off, s->d_sc + (size_t)q * nch, nch * sizeof(int), cudaMemcpyDeviceToHost, cs));
+    CKR(cudaMemcpyAsync(s->h_ns + off, s->d_ns + (size_t)q * nch, nch * sizeof(int), cudaMemcpyDeviceToHost, cs));
     return TSA_OK;
   };
   // enqueue on stream cs: copy global chain g's record out of buffer buf into the pinned best record
+  // (broadcast from its owner, or, scoring locally, a copy of this rank's own chain)
   auto fetch_best = [&](int g, uint8_t* buf, cudaStream_t cs) -> int {
     s->d2h += rb;
-    if (s->world > 1)
+    if (s->world > 1 && !local)
       return s->comm->fetch_record(buf + (size_t)(g % nch) * rb, rb, g / nch, s->h_best, cs, err, errlen);
-    CKR(cudaMemcpyAsync(s->h_best, buf + (size_t)g * rb, rb, cudaMemcpyDeviceToHost, cs));
+    CKR(cudaMemcpyAsync(s->h_best, buf + (size_t)(g - s->rank * nch) * rb, rb, cudaMemcpyDeviceToHost, cs));
     return TSA_OK;
   };
   auto check_err = [&]() -> int {
@@ -967,7 +1049,11 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         const int q = (int)(pend & 1);
         CKR(cudaEventSynchronize(s->eve[q]));
         int improved;
-        process((size_t)pend, s->h_lc + (size_t)q * ng, s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng, &improved);
+        if (local)
+          process_local((size_t)pend, q, &improved);
+        else
+          process((size_t)pend, s->h_lc + (size_t)q * ng, s->h_sc + (size_t)q * ng, s->h_ns + (size_t)q * ng,
+                  &improved);
         if (improved >= 0) rc = fetch_best(improved, buf[q ^ 1], s->cst);  // level pend's output buffer
         if (rc == TSA_OK) CKR(cudaEventRecord(s->evfree[q], s->cst));
         pend = -1;
@@ -1042,7 +1128,10 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       const float* glc = s->h_lc;
       const int *gsc = s->h_sc, *gns = s->h_ns;
       int improved;
-      process(lev, glc, gsc, gns, &improved);
+      if (local)
+        process_local(lev, 0, &improved);
+      else
+        process(lev, glc, gsc, gns, &improved);
       if (improved >= 0) {
         if ((rc = fetch_best(improved, s->d_cur, s->st))) break;
         CKR(cudaStreamSynchronize(s->st));
@@ -1097,6 +1186,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   CKR(cudaStreamSynchronize(s->st));
   CKR(cudaStreamSynchronize(s->cst));
   if ((rc = check_err())) return rc;
+  if (local && (rc = reduce_local())) return rc;
   memcpy(s->best.data(), s->h_best, rb);
   // the energies of the last level, this rank's chains
   {
