@@ -202,6 +202,12 @@ int tsa_session_energies(tsa_session* s, float* lcost, int32_t* sc, int32_t* ns,
  * to host buffers (either may be NULL), for tests. */
 int tsa_session_chains(tsa_session* s, uint32_t* trees, uint64_t* labels, char* err, size_t errlen);
 
+/* Free the device and pinned host blocks that finished sessions left in the library's block cache
+ * (kept so that repeated tsa_run calls of one workload skip the allocations; at most 8 GiB of device
+ * memory and 1 GiB of pinned memory are held).  Safe to call at any time; live sessions keep theirs.
+ * No counterpart in the reference, which allocates per run (csrc/treesa_gpu.cu:1565-1577). */
+int tsa_release_cached_memory(void);
+
 /* Multi-GPU rendezvous: write a fresh 128-byte ncclUniqueId into id (rank 0 calls it and shares the
  * bytes with the other ranks, e.g. through torch.distributed). */
 int tsa_nccl_unique_id(void* id128, char* err, size_t errlen);

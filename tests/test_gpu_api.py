@@ -79,3 +79,19 @@ def test_optimize_multi_on_one_gpu():
     tree, best, infos = tg.optimize_multi(ixs, [], gpus=[0, 0, 0], nchains=256, niters=4, sc_target=30)
     tcs = [i["tc_total_py"] for i in infos]
     assert all(i["valid"] for i in infos) and best["tc_total_py"] == min(tcs) and len(set(tcs)) > 1
+
+
+def test_block_cache_reuse_keeps_results():
+    """tsa_run reuses a finished call's device and pinned blocks (stale contents included): repeated calls,
+    calls of another size in between and a call after tsa_release_cached_memory return the same tree."""
+    from treesa_gpu_b200 import _abi
+    rec = _util.instance("sat40")
+    kw = dict(nchains=96, niters=3, sc_target=30, init="random", seed=5)
+    t0, i0 = tg.optimize(rec["ixs"], rec["iy"], **kw)
+    tg.optimize(rec["ixs"], rec["iy"], **dict(kw, nchains=200, seed=9))
+    t1, i1 = tg.optimize(rec["ixs"], rec["iy"], **kw)
+    assert _abi.lib().tsa_release_cached_memory() == 0
+    t2, i2 = tg.optimize(rec["ixs"], rec["iy"], **kw)
+    assert t0 == t1 == t2
+    assert (i0["tc"], i0["sc"], i0["proposals"]) == (i1["tc"], i1["sc"], i1["proposals"]) == \
+        (i2["tc"], i2["sc"], i2["proposals"])

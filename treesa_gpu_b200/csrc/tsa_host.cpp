@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <chrono>
 #include <functional>
+#include <map>
 #include <mutex>
 #include <numeric>
 #include <random>
@@ -48,6 +49,78 @@ void set_err(char* err, size_t n, const char* fmt, ...) {
       return TSA_ERR_CUDA;                                                                     \
     }                                                                                          \
   } while (0)
+
+// Process-wide cache of device and pinned host blocks.  One-shot tsa_run calls of one workload reuse the
+// previous call's buffers instead of paying cudaMalloc / cudaMallocHost and the synchronizing frees on
+// every call.  A freed block is kept for a later request of the same (device, kind, size) while the
+// cache holds at most kPoolCap[kind] bytes; tsa_release_cached_memory() empties it.  Blocks go back to
+// the cache only after the session's streams are idle.
+struct BlockPool {
+  static constexpr size_t kPoolCap[2] = {size_t(8) << 30, size_t(1) << 30};  // device, pinned host
+  struct Key {
+    int device, kind;
+    size_t bytes;
+    bool operator<(const Key& o) const { return std::tie(device, kind, bytes) < std::tie(o.device, o.kind, o.bytes); }
+  };
+  std::mutex mu;
+  std::multimap<Key, void*> idle;
+  std::map<void*, Key> live;
+  size_t held[2] = {0, 0};
+};
+BlockPool& block_pool() {
+  static BlockPool* P = new BlockPool();  // never destroyed: blocks may outlive static destruction order
+  return *P;
+}
+void raw_free(int kind, void* p) {
+  if (kind == 0)
+    cudaFree(p);
+  else
+    cudaFreeHost(p);
+}
+// kind 0: device memory of the current device; 1: pinned host memory
+cudaError_t pool_alloc(int kind, void** out, size_t bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  bytes = std::max<size_t>(bytes, 1);
+  BlockPool& P = block_pool();
+  const BlockPool::Key k{kind == 0 ? dev : -1, kind, bytes};
+  {
+    std::lock_guard<std::mutex> g(P.mu);
+    auto it = P.idle.find(k);
+    if (it != P.idle.end()) {
+      *out = it->second;
+      P.idle.erase(it);
+      P.held[kind] -= bytes;
+      P.live[*out] = k;
+      return cudaSuccess;
+    }
+  }
+  e = kind == 0 ? cudaMalloc(out, bytes) : cudaMallocHost(out, bytes);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(P.mu);
+  P.live[*out] = k;
+  return cudaSuccess;
+}
+template <typename T>
+cudaError_t pool_alloc(int kind, T** out, size_t bytes) {
+  return pool_alloc(kind, reinterpret_cast<void**>(out), bytes);
+}
+void pool_free(void* p) {
+  if (!p) return;
+  BlockPool& P = block_pool();
+  std::lock_guard<std::mutex> g(P.mu);
+  auto it = P.live.find(p);
+  if (it == P.live.end()) return;
+  const BlockPool::Key k = it->second;
+  P.live.erase(it);
+  if (P.held[k.kind] + k.bytes <= BlockPool::kPoolCap[k.kind]) {
+    P.idle.emplace(k, p);
+    P.held[k.kind] += k.bytes;
+  } else {
+    raw_free(k.kind, p);
+  }
+}
 
 double now_s() {
   return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
@@ -469,18 +542,12 @@ struct tsa_session {
 
   ~tsa_session() {
     if (device >= 0) cudaSetDevice(device);
-    cudaFree(d_rec);
-    cudaFree(d_rec2);
-    cudaFree(d_init);
-    cudaFree(d_leaf);
-    cudaFree(d_leaf_sum);
-    cudaFree(d_lse);
-    cudaFree(d_lc);
-    cudaFree(d_sc);
-    cudaFree(d_ns);
-    cudaFree(d_anc);
-    cudaFree(d_err);
-    cudaFree(d_stats);
+    if (st) cudaStreamSynchronize(st);  // nothing in flight touches the blocks handed back to the cache
+    if (cst) cudaStreamSynchronize(cst);
+    for (void* p : {(void*)d_rec, (void*)d_rec2, (void*)d_init, (void*)d_leaf, (void*)d_leaf_sum, (void*)d_lse,
+                    (void*)d_lc, (void*)d_sc, (void*)d_ns, (void*)d_anc, (void*)d_err, (void*)d_stats, (void*)h_lc,
+                    (void*)h_sc, (void*)h_ns, (void*)h_best})
+      pool_free(p);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (auto& e : evk)
@@ -492,10 +559,6 @@ struct tsa_session {
     for (auto& e : evfree)
       if (e) cudaEventDestroy(e);
     if (cst) cudaStreamDestroy(cst);
-    cudaFreeHost(h_lc);
-    cudaFreeHost(h_sc);
-    cudaFreeHost(h_ns);
-    cudaFreeHost(h_best);
     if (own_stream && st) cudaStreamDestroy(st);
     delete comm;
   }
@@ -534,33 +597,33 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
     return TSA_ERR_UNSUPPORTED;
   }
   const size_t recb = (size_t)s->L.rec_bytes * s->nchains;
-  CKR(cudaMalloc(&s->d_rec, recb));
-  CKR(cudaMalloc(&s->d_init, recb));
-  CKR(cudaMalloc(&s->d_rec2, recb));
-  CKR(cudaMalloc(&s->d_leaf, s->I.leaf.size() * 8));
-  CKR(cudaMalloc(&s->d_lse, 64 * sizeof(float)));
-  CKR(cudaMalloc(&s->d_lc, 2 * s->nchains * sizeof(float)));
-  CKR(cudaMalloc(&s->d_sc, 2 * s->nchains * sizeof(int)));
-  CKR(cudaMalloc(&s->d_ns, 2 * s->nchains * sizeof(int)));
-  CKR(cudaMallocHost(&s->h_lc, 2 * (size_t)s->nglobal * sizeof(float)));
-  CKR(cudaMallocHost(&s->h_sc, 2 * (size_t)s->nglobal * sizeof(int)));
-  CKR(cudaMallocHost(&s->h_ns, 2 * (size_t)s->nglobal * sizeof(int)));
-  CKR(cudaMallocHost(&s->h_best, s->L.rec_bytes));
+  CKR(pool_alloc(0, &s->d_rec, recb));
+  CKR(pool_alloc(0, &s->d_init, recb));
+  CKR(pool_alloc(0, &s->d_rec2, recb));
+  CKR(pool_alloc(0, &s->d_leaf, s->I.leaf.size() * 8));
+  CKR(pool_alloc(0, &s->d_lse, 64 * sizeof(float)));
+  CKR(pool_alloc(0, &s->d_lc, 2 * s->nchains * sizeof(float)));
+  CKR(pool_alloc(0, &s->d_sc, 2 * s->nchains * sizeof(int)));
+  CKR(pool_alloc(0, &s->d_ns, 2 * s->nchains * sizeof(int)));
+  CKR(pool_alloc(1, &s->h_lc, 2 * (size_t)s->nglobal * sizeof(float)));
+  CKR(pool_alloc(1, &s->h_sc, 2 * (size_t)s->nglobal * sizeof(int)));
+  CKR(pool_alloc(1, &s->h_ns, 2 * (size_t)s->nglobal * sizeof(int)));
+  CKR(pool_alloc(1, &s->h_best, s->L.rec_bytes));
   for (auto& e : s->evk) CKR(cudaEventCreate(&e));
   for (auto& e : s->eve) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : s->evdone) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : s->evfree) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   CKR(cudaStreamCreateWithFlags(&s->cst, cudaStreamNonBlocking));
-  CKR(cudaMalloc(&s->d_anc, s->nchains * sizeof(int)));
-  CKR(cudaMalloc(&s->d_err, sizeof(int)));
-  CKR(cudaMalloc(&s->d_stats, 10 * sizeof(unsigned long long)));
+  CKR(pool_alloc(0, &s->d_anc, s->nchains * sizeof(int)));
+  CKR(pool_alloc(0, &s->d_err, sizeof(int)));
+  CKR(pool_alloc(0, &s->d_stats, 10 * sizeof(unsigned long long)));
   CKR(cudaEventCreate(&s->ev0));
   CKR(cudaEventCreate(&s->ev1));
   CKR(cudaMemcpyAsync(s->d_leaf, s->I.leaf.data(), s->I.leaf.size() * 8, cudaMemcpyHostToDevice, s->st));
   {
     std::vector<uint64_t> ls(s->I.m, 0);
     if (s->L.sums) fill_sums(s->I.leaf.data(), s->I.m, s->L.nw, ls.data());
-    CKR(cudaMalloc(&s->d_leaf_sum, ls.size() * 8));
+    CKR(pool_alloc(0, &s->d_leaf_sum, ls.size() * 8));
     CKR(cudaMemcpy(s->d_leaf_sum, ls.data(), ls.size() * 8, cudaMemcpyHostToDevice));
     s->h2d += ls.size() * 8;
   }
@@ -1388,6 +1451,21 @@ int tsa_session_chains(tsa_session* s, uint32_t* trees, uint64_t* labels, char* 
     if (trees) memcpy(trees + (size_t)c * L.nint, rec + L.off_ch, (size_t)L.nint * 4);
     if (labels) memcpy(labels + (size_t)c * L.nint * L.nw, rec, (size_t)L.nint * L.nw * 8);
   }
+  return TSA_OK;
+}
+
+int tsa_release_cached_memory(void) {
+  BlockPool& P = block_pool();
+  std::lock_guard<std::mutex> g(P.mu);
+  int dev0 = -1;
+  cudaGetDevice(&dev0);
+  for (auto& kv : P.idle) {
+    if (kv.first.kind == 0) cudaSetDevice(kv.first.device);
+    raw_free(kv.first.kind, kv.second);
+  }
+  P.idle.clear();
+  P.held[0] = P.held[1] = 0;
+  if (dev0 >= 0) cudaSetDevice(dev0);
   return TSA_OK;
 }
 
