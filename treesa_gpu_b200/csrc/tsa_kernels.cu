@@ -1813,17 +1813,13 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     }
     if (lane == 31) F.scan[warp] = incl;
     __syncthreads();
-    if (warp == 0) {
-      int v = lane < nwarps ? F.scan[lane] : 0;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xFFFFFFFFu, v, o);
-        if (lane >= o) v += t;
-      }
-      F.scan[lane] = v;
+    int total, before;
+    {  // every warp sums the warp totals itself (no second barrier)
+      const int v = lane < nwarps ? F.scan[lane] : 0;
+      total = __reduce_add_sync(0xFFFFFFFFu, v);
+      before = __reduce_add_sync(0xFFFFFFFFu, lane < warp ? v : 0);
     }
-    __syncthreads();
-    if (tid < nb) F.off[tid] = (uint32_t)(incl - nck + (warp ? F.scan[warp - 1] : 0));
-    const int total = F.scan[nwarps - 1];
+    if (tid < nb) F.off[tid] = (uint32_t)(incl - nck + before);
     __syncthreads();
     // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first two items.  A batch of
     // at most 2T items decodes each item's node and chunk directly (no list)
@@ -1924,7 +1920,10 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
         if (F.acc[it.j]) flat_store(B, F, it, flat_eval<CL>(B, F, wlb, it).x);
       }
     }
-    __syncthreads();
+    // The next batch rewrites the tables at once, so it waits for the stores.  After the last batch the
+    // caller's next phase writes wl and the tables only behind its own scan barrier, and the stores of a
+    // batch of at most 2T items read neither (X and the items come from registers): no barrier then.
+    if (b0 + NB < nk || total > 2 * T) __syncthreads();
   }
 }
 
@@ -2040,12 +2039,12 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
         int nU = nint;
         const bool follow = a.par_follow != 0;
         const int max_phases = follow ? 2 * nint : nint;
+        // the scan counters alternate between sh[0..1] (even phases) and sh[2..3] (odd phases): a phase
+        // clears the next phase's pair behind its own scan barrier, so no barrier is spent on clearing
+        if (tid == 0) sh[0] = sh[1] = sh[2] = sh[3] = 0;
+        __syncthreads();
         for (int guard = 0; guard <= max_phases; guard++) {
-          if (tid == 0) {
-            sh[0] = 0;
-            sh[1] = 0;
-          }
-          __syncthreads();
+          int* const ctr = sh + 2 * (guard & 1);
           for (int base = 0; base < nU; base += T) {
             int j = base + tid;
             bool valid = j < nU;
@@ -2073,8 +2072,8 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
             unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
             int pa = 0, pk = 0;
             if (lane == 0) {
-              if (ba) pa = atomicAdd(&sh[0], __popc(ba));
-              if (bk) pk = atomicAdd(&sh[1], __popc(bk));
+              if (ba) pa = atomicAdd(&ctr[0], __popc(ba));
+              if (bk) pk = atomicAdd(&ctr[1], __popc(bk));
             }
             pa = __shfl_sync(FULL, pa, 0);
             pk = __shfl_sync(FULL, pk, 0);
@@ -2082,15 +2081,16 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
             if (valid && !act) U2[pk + __popc(bk & lt)] = (uint16_t)q;
           }
           __syncthreads();
-          const int nk = sh[0];
-          nU = sh[1];
+          const int nk = ctr[0];
+          nU = ctr[1];
+          if (tid == 0) sh[2 * ((guard + 1) & 1)] = sh[2 * ((guard + 1) & 1) + 1] = 0;
           uint16_t* tmp = U;
           U = U2;
           U2 = tmp;
           if (nk == 0) break;
           if (tid == 0) cnt.steps++;
-          // re-armed pivots (par_follow) are appended to U after the nU kept nodes, counted on in sh[1]
-          const FollowCtx fctx{pri, U, &sh[1], hs};
+          // re-armed pivots (par_follow) are appended to U after the nU kept nodes, counted on in ctr[1]
+          const FollowCtx fctx{pri, U, &ctr[1], hs};
           const FollowCtx* fol = follow ? &fctx : nullptr;
           if constexpr (SUMS && !MODEL) {
             par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{}, fol);
@@ -2111,10 +2111,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
             }
             __syncthreads();
           }
-          if (follow) {
-            nU = sh[1];
-            __syncthreads();  // every thread has read the count before the next phase clears it
-          }
+          if (follow) nU = ctr[1];  // cleared again only behind the next phase's scan barrier
         }
       } else {
         if (tid == 0) {
@@ -2222,7 +2219,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
   const unsigned FULL = 0xFFFFFFFFu;
   float* s_lse = reinterpret_cast<float*>(smem);
   double* s_exp = reinterpret_cast<double*>(smem + 256);
-  int* sh = reinterpret_cast<int*>(smem + 768);  // [0,2) scan counters, [4,6) the peer's active counts
+  int* sh = reinterpret_cast<int*>(smem + 768);  // [0,4) scan counters (a pair per phase parity), [4,6) the peer's active counts
   for (int q = tid; q < 64; q += T) {
     s_lse[q] = a.lse_tab[q];
     s_exp[q] = c_exp_tab[q];
@@ -2317,14 +2314,12 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
       int nU = (nint - rank + 1) / 2;  // the nodes q = 2j + rank
       for (int j = tid; j < nU; j += T) Ua[j] = (uint16_t)(2 * j + rank);
       uint16_t *U = Ua, *U2 = Ub;
+      // scan counters alternate between sh[0..1] and sh[2..3] by phase (cleared behind the scan barrier)
+      if (tid == 0) sh[0] = sh[1] = sh[2] = sh[3] = 0;
       // both copies are complete (loaded or initialised) before either CTA writes into the other
       cl.sync();
       for (int guard = 0; guard <= nint; guard++, ph++) {
-        if (tid == 0) {
-          sh[0] = 0;
-          sh[1] = 0;
-        }
-        __syncthreads();
+        int* const ctr = sh + 2 * (guard & 1);
         for (int base = 0; base < nU; base += T) {
           int j = base + tid;
           bool valid = j < nU;
@@ -2352,8 +2347,8 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
           unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
           int pa = 0, pk = 0;
           if (lane == 0) {
-            if (ba) pa = atomicAdd(&sh[0], __popc(ba));
-            if (bk) pk = atomicAdd(&sh[1], __popc(bk));
+            if (ba) pa = atomicAdd(&ctr[0], __popc(ba));
+            if (bk) pk = atomicAdd(&ctr[1], __popc(bk));
           }
           pa = __shfl_sync(FULL, pa, 0);
           pk = __shfl_sync(FULL, pk, 0);
@@ -2361,8 +2356,9 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
           if (valid && !act) U2[pk + __popc(bk & lt)] = (uint16_t)q;
         }
         __syncthreads();
-        const int nk = sh[0];
-        nU = sh[1];
+        const int nk = ctr[0];
+        nU = ctr[1];
+        if (tid == 0) sh[2 * ((guard + 1) & 1)] = sh[2 * ((guard + 1) & 1) + 1] = 0;
         uint16_t* tmp = U;
         U = U2;
         U2 = tmp;
