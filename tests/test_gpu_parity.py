@@ -228,6 +228,32 @@ def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
         assert abs(od["tc"] - d["tc"]) < 1e-9 and od["sc"] == d["sc"]
 
 
+@pytest.mark.parametrize("name,order", [("grid24", "par"), ("grid24", "preorder"), ("sq46", "par")])
+def test_block_kernel_two_ctas_per_sm(name, order):
+    """More chains than SMs: the CTA-per-chain kernel runs two 8-warp CTAs per SM.  A chain's trajectory
+    depends only on its global id, so chains from the first and the last wave are checked against the
+    oracle run on those chains alone."""
+    import torch
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    rec = _util.instance(name)
+    net, onet = _net(rec)
+    nch = nsm + 12
+    trees = _util.start_trees(rec, nch, seed=7)
+    betas = CHECK_BETAS[:4]
+    s = engine.Session(net, betas=betas, niters=2, nchains=nch, sc_target=24.0, order=order, seed=7,
+                       init_trees=trees, kernel_hint="block")
+    info = s.info()
+    assert info["kernel"] == 2 and info["warps_per_cta"] == 8, info
+    s.run()
+    t, lab = s.chains()
+    s.close()
+    nw = onet.nw
+    for c0 in (0, nsm - 2, nch - 4):
+        ot, olab, _ = O.sweeps(onet, trees[c0:c0 + 4], betas, 2, order=order, seed=7, sc_target=24.0, c0=c0)
+        assert (t[c0:c0 + 4] == ot).all(), c0
+        assert (lab[c0:c0 + 4, :, :nw] == olab).all(), c0
+
+
 @pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
 @pytest.mark.parametrize("name", ["sat100", "reg3_250", "grid24", "sq46"])
 def test_fixed_slice_set_bit_exact(name, kernel):
