@@ -17,7 +17,9 @@
 //
 // k_anneal_cluster: par order with chunk summaries when chains are fewer than half the SMs (the 64x64
 // lattice: 72 chains of 4 MB): a cluster of two CTAs per chain, metadata replicated in both CTAs'
-// shared memory and kept equal by distributed-shared-memory stores, one cluster barrier per phase.
+// shared memory and kept equal by distributed-shared-memory stores; per phase the CTAs meet at a split
+// cluster barrier (arrive after the scan, wait before the first store into the other copy) and at a full
+// one at its end.
 //
 // Every kernel produces bit-identical trees to the reference's CPU port (csrc/cpu_ref.h) for the same
 // Philox counters; see tsa_core.h for the arithmetic.
@@ -1254,6 +1256,10 @@ __device__ __forceinline__ ulonglong2 ld2_cg(const uint64_t* p) {
                : "memory");
   return r;
 }
+// Split cluster barrier: arrive (release) after the phase's scan, wait (acquire) before the first write
+// into the other CTA's shared memory.  Every thread of both CTAs executes each, in the same order.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // The other CTA's copies of the replicated per-node arrays of a CTA pair, each mapped with
 // map_shared_rank (distributed shared memory; null for a single CTA).  Always indexed from these bases:
 // a local shared-memory pointer plus an offset would keep the shared state space and miss the peer.
@@ -1862,6 +1868,9 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       }
     }
     __syncthreads();
+    // a CTA pair: the other CTA has finished this phase's scan before any metadata is rewritten in its
+    // copy (the caller arrived at the cluster barrier after its own scan)
+    if (CL == 2 && b0 == 0) cluster_wait();
     // 4. owners: energy, Metropolis, metadata
     if (tid < nb) {
       bool acc = false;
@@ -2204,9 +2213,11 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
 // the GPU idle; here both CTAs of a pair hold a full copy of the chain's per-node metadata in their own
 // shared memory, and every metadata write of a visit goes to both copies (a distributed-shared-memory
 // store).  CTA r owns the nodes q with q % 2 == r: it scans them for the phase's independent set and
-// visits the active ones with par_phase_flat; label sets stay in HBM (loaded L2-only).  The two CTAs
-// meet at one cluster barrier per phase, which also exchanges their active counts; the phase sequence
-// and every move are those of k_anneal_block, so the chains are bit-identical.
+// visits the active ones with par_phase_flat; label sets stay in HBM (loaded L2-only).  Per phase the
+// two CTAs meet at a split cluster barrier (each arrives after its scan and waits before its first store
+// into the other's copy, so no scan reads a word the phase rewrites) and at a full one at the end, which
+// also exchanges their active counts; the phase sequence and every move are those of k_anneal_block,
+// so the chains are bit-identical.
 // ================================================================================================
 __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
   namespace cg = cooperative_groups;
@@ -2362,7 +2373,12 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
         uint16_t* tmp = U;
         U = U2;
         U2 = tmp;
-        if (nk > 0) par_phase_flat<true, 2>(B, F, wl, pri, par, nk, sw, chain, cnt, P);
+        // this CTA's scan is done: the other CTA may rewrite this copy's metadata once it has waited
+        cluster_arrive();
+        if (nk > 0)
+          par_phase_flat<true, 2>(B, F, wl, pri, par, nk, sw, chain, cnt, P);  // waits before its writes
+        else
+          cluster_wait();
         if (tid == 0) peer_sh[4 + (ph & 1)] = nk;
         cl.sync();
         const int total = nk + sh[4 + (ph & 1)];
