@@ -1599,6 +1599,66 @@ __device__ void slice_step_block(const BlkCtx& B, const SweepArgs& a, uint32_t* 
   (void)shf;
 }
 
+// One par phase's scan of a CTA's unvisited list U[0, nU) (csrc/cpu_ref.h:154-166): a node is active iff
+// its key pri << 16 | id exceeds the key of every unvisited neighbour (parent, internal children; a
+// visited node has pri 0, so its key is below every unvisited key).  Active nodes are appended to wl,
+// the others to U2, at places reserved through the counters ctr[0] and ctr[1].  Each thread takes up to R
+// entries per round with all their shared-memory loads issued together (a missing neighbour reads the
+// node's own key, which blocks nothing), and a warp reserves its places for the whole round with one
+// atomic per list.
+template <int R>
+__device__ __forceinline__ void phase_scan(const uint16_t* U, int nU, uint16_t* wl, uint16_t* U2, int* ctr,
+                                           const uint16_t* pri, const uint16_t* par, const uint32_t* ch, int m) {
+  const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31;
+  const unsigned FULL = 0xFFFFFFFFu, lt = (1u << lane) - 1u;
+  for (int base = 0; base < nU; base += R * T) {
+    int q[R];
+    bool valid[R], act[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const int j = base + r * T + tid;
+      valid[r] = j < nU;
+      q[r] = valid[r] ? (int)U[j] : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint32_t own = (uint32_t)(m + q[r]);
+      const uint32_t key = ((uint32_t)pri[q[r]] << 16) | own;
+      const int p = par[q[r]];
+      const uint32_t cw = ch[q[r]];
+      const int l = (int)(cw & 0xFFFFu), rr = (int)(cw >> 16);
+      const uint32_t np = p != 0xFFFF ? (uint32_t)p : own, nl = l >= m ? (uint32_t)l : own,
+                     nr = rr >= m ? (uint32_t)rr : own;
+      const uint32_t kp = ((uint32_t)pri[np - m] << 16) | np, kl = ((uint32_t)pri[nl - m] << 16) | nl,
+                     kr = ((uint32_t)pri[nr - m] << 16) | nr;
+      act[r] = valid[r] && key >= kp && key >= kl && key >= kr;  // ids differ: equal only for the node itself
+    }
+    unsigned ba[R], bk[R];
+    int ta = 0, tk = 0;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      ba[r] = __ballot_sync(FULL, act[r]);
+      bk[r] = __ballot_sync(FULL, valid[r] && !act[r]);
+      ta += __popc(ba[r]);
+      tk += __popc(bk[r]);
+    }
+    int pa = 0, pk = 0;
+    if (lane == 0) {
+      if (ta) pa = atomicAdd(&ctr[0], ta);
+      if (tk) pk = atomicAdd(&ctr[1], tk);
+    }
+    pa = __shfl_sync(FULL, pa, 0);
+    pk = __shfl_sync(FULL, pk, 0);
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      if (act[r]) wl[pa + __popc(ba[r] & lt)] = (uint16_t)q[r];
+      if (valid[r] && !act[r]) U2[pk + __popc(bk[r] & lt)] = (uint16_t)q[r];
+      pa += __popc(ba[r]);
+      pk += __popc(bk[r]);
+    }
+  }
+}
+
 __device__ __forceinline__ int pick_group(int k, int T) {
   int G = 32;
   while (G > 1 && k * G > T) G >>= 1;
@@ -1980,7 +2040,6 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
   float* costs = reinterpret_cast<float*>(Ua);  // model modes: node costs, while the U lists are free
   const int m = L.m, nint = L.nint;
-  const unsigned lt = (1u << lane) - 1u;
   FlatTabs F;
   F.info = reinterpret_cast<uint2*>(smem + Bm.off_ninfo);
   F.rnd = reinterpret_cast<uint32_t*>(smem + Bm.off_nrnd);
@@ -2054,41 +2113,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
         __syncthreads();
         for (int guard = 0; guard <= max_phases; guard++) {
           int* const ctr = sh + 2 * (guard & 1);
-          for (int base = 0; base < nU; base += T) {
-            int j = base + tid;
-            bool valid = j < nU;
-            int q = valid ? (int)U[j] : 0;
-            bool act = false;
-            if (valid) {
-              uint32_t key = ((uint32_t)pri[q] << 16) | (uint32_t)(m + q);
-              act = true;
-              int p = par[q];
-              if (p != 0xFFFF) {
-                uint32_t pp = pri[p - m];
-                if (pp && ((pp << 16) | (uint32_t)p) > key) act = false;
-              }
-              uint32_t cw = B.ch[q];
-              int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
-              if (act && l >= m) {
-                uint32_t pl = pri[l - m];
-                if (pl && ((pl << 16) | (uint32_t)l) > key) act = false;
-              }
-              if (act && r >= m) {
-                uint32_t pr = pri[r - m];
-                if (pr && ((pr << 16) | (uint32_t)r) > key) act = false;
-              }
-            }
-            unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
-            int pa = 0, pk = 0;
-            if (lane == 0) {
-              if (ba) pa = atomicAdd(&ctr[0], __popc(ba));
-              if (bk) pk = atomicAdd(&ctr[1], __popc(bk));
-            }
-            pa = __shfl_sync(FULL, pa, 0);
-            pk = __shfl_sync(FULL, pk, 0);
-            if (act) wl[pa + __popc(ba & lt)] = (uint16_t)q;
-            if (valid && !act) U2[pk + __popc(bk & lt)] = (uint16_t)q;
-          }
+          phase_scan<4>(U, nU, wl, U2, ctr, pri, par, B.ch, m);
           __syncthreads();
           const int nk = ctr[0];
           nU = ctr[1];
@@ -2263,7 +2288,6 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
   uint16_t* Ua = reinterpret_cast<uint16_t*>(smem + Bm.off_U);
   uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
   const int m = L.m, nint = L.nint;
-  const unsigned lt = (1u << lane) - 1u;
   FlatTabs F;
   F.info = reinterpret_cast<uint2*>(smem + Bm.off_ninfo);
   F.rnd = reinterpret_cast<uint32_t*>(smem + Bm.off_nrnd);
@@ -2331,41 +2355,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
       cl.sync();
       for (int guard = 0; guard <= nint; guard++, ph++) {
         int* const ctr = sh + 2 * (guard & 1);
-        for (int base = 0; base < nU; base += T) {
-          int j = base + tid;
-          bool valid = j < nU;
-          int q = valid ? (int)U[j] : 0;
-          bool act = false;
-          if (valid) {
-            uint32_t key = ((uint32_t)pri[q] << 16) | (uint32_t)(m + q);
-            act = true;
-            int p = par[q];
-            if (p != 0xFFFF) {
-              uint32_t pp = pri[p - m];
-              if (pp && ((pp << 16) | (uint32_t)p) > key) act = false;
-            }
-            uint32_t cw = B.ch[q];
-            int l = (int)(cw & 0xFFFFu), r = (int)(cw >> 16);
-            if (act && l >= m) {
-              uint32_t pl = pri[l - m];
-              if (pl && ((pl << 16) | (uint32_t)l) > key) act = false;
-            }
-            if (act && r >= m) {
-              uint32_t pr = pri[r - m];
-              if (pr && ((pr << 16) | (uint32_t)r) > key) act = false;
-            }
-          }
-          unsigned ba = __ballot_sync(FULL, act), bk = __ballot_sync(FULL, valid && !act);
-          int pa = 0, pk = 0;
-          if (lane == 0) {
-            if (ba) pa = atomicAdd(&ctr[0], __popc(ba));
-            if (bk) pk = atomicAdd(&ctr[1], __popc(bk));
-          }
-          pa = __shfl_sync(FULL, pa, 0);
-          pk = __shfl_sync(FULL, pk, 0);
-          if (act) wl[pa + __popc(ba & lt)] = (uint16_t)q;
-          if (valid && !act) U2[pk + __popc(bk & lt)] = (uint16_t)q;
-        }
+        phase_scan<4>(U, nU, wl, U2, ctr, pri, par, B.ch, m);
         __syncthreads();
         const int nk = ctr[0];
         nU = ctr[1];
