@@ -48,3 +48,23 @@ def digest(trees, labels):
     h.update(np.ascontiguousarray(trees, np.uint32).tobytes())
     h.update(np.ascontiguousarray(labels, np.uint64).tobytes())
     return h.hexdigest()
+
+
+def ring(n):
+    return [[i, (i + 1) % n] for i in range(n)], []
+
+
+# small and degenerate networks, and label counts at the packed-word boundaries (1, 2, 3->4, 8 and 9->10
+# words): three tensors, an empty tensor, disconnected parts (outer products), open legs, a star
+EDGE = {
+    "triangle": ([[0, 1], [1, 2], [2, 0]], []),
+    "empty_tensor": ([[0, 1], [], [1, 2], [2, 0]], []),
+    "disconnected": ([[0], [0], [1], [1], [2, 3], [3]], []),
+    "open_legs": ([[0, 5], [0, 1, 6], [1, 7], [7, 5]], [5, 6]),
+    "star": ([[0, 1, 2, 3], [0], [1], [2], [3]], []),
+    "ring64": ring(64),
+    "ring65": ring(65),
+    "ring129": ring(129),
+    "ring512": ring(512),
+    "ring513": ring(513),
+}

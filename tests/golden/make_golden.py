@@ -19,7 +19,11 @@ Writes
                      (d) as (b) in par order with the CLI's --par-band L and --par-follow variants
                      (csrc/cpu_ref.h:140-175);
                      (e) as (b) with the energy modes gpu and h100 (ref_*<1>, ref_*<2>, default model
-                     constants), both orders.
+                     constants), both orders;
+                     (f) small and degenerate networks (tests/_util.EDGE: three tensors, an empty
+                     tensor, disconnected parts, open legs, a star, rings at the packed-word
+                     boundaries), 16 random start trees, betas 0.5/1/2/4 x 3 sweeps, sc_target 2, seed 3,
+                     both orders.
 """
 import hashlib
 import json
@@ -135,6 +139,19 @@ def main(ref):
                                   sc_target=24.0, nchains=8, proposals=int(cnt[0]), accepts=int(cnt[1]),
                                   sha256=digest(t, l)))
 
+    # (f) small and degenerate networks
+    from tests import _util
+    edge = []
+    ebetas = np.array([0.5, 1.0, 2.0, 4.0], np.float32)
+    for name, (ixs, iy) in _util.EDGE.items():
+        nlab = 1 + max(l for ix in ixs for l in ix)
+        net = O.Net(ixs, iy, nlab)
+        trees = np.stack([O.random_tree(net.m, 3, c) for c in range(16)])
+        for order in ("par", "preorder"):
+            t, l, cnt, _ = O.ref_sweeps(net, trees, ebetas, 3, order=order, seed=3, sc_target=2.0)
+            edge.append(dict(instance=name, order=order, betas=[0.5, 1.0, 2.0, 4.0], niters=3, seed=3, sc_target=2.0,
+                             nchains=16, proposals=int(cnt[0]), accepts=int(cnt[1]), sha256=digest(t, l)))
+
     # (c) sq32 / sq48 from the row-major path tree (tc / sc identical on RTX 6000 and H100)
     large = []
     for line in open(os.path.join(ref, "bench", "results", "large_compare_gpu_par.jsonl")):
@@ -143,9 +160,9 @@ def main(ref):
             large.append(dict(instance=r["instance"], nchains=r["nchains"], niters=r["niters"], beta0=r["beta0"],
                               tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
     with open(os.path.join(HERE, "expected.json"), "w") as f:
-        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes), f, indent=1)
+        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes, edge=edge), f, indent=1)
     print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}, "
-          f"variants {len(variants)}, modes {len(modes)}")
+          f"variants {len(variants)}, modes {len(modes)}, edge {len(edge)}")
 
 
 if __name__ == "__main__":

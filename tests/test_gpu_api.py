@@ -95,3 +95,12 @@ def test_block_cache_reuse_keeps_results():
     assert t0 == t1 == t2
     assert (i0["tc"], i0["sc"], i0["proposals"]) == (i1["tc"], i1["sc"], i1["proposals"]) == \
         (i2["tc"], i2["sc"], i2["proposals"])
+
+
+@pytest.mark.parametrize("name", ["triangle", "empty_tensor", "disconnected", "open_legs", "star", "ring65"])
+def test_optimize_edge_networks(name):
+    """Small and degenerate networks end to end: a valid tree whose reported costs match trees.py."""
+    ixs, iy = _util.EDGE[name]
+    tree, info = tg.optimize(ixs, iy, nchains=64, niters=3, sc_target=10, init="random")
+    _check(tree, info, ixs, iy, len(ixs))
+

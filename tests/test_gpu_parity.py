@@ -228,6 +228,28 @@ def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
         assert abs(od["tc"] - d["tc"]) < 1e-9 and od["sc"] == d["sc"]
 
 
+@pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
+@pytest.mark.parametrize("order", ["par", "preorder"])
+@pytest.mark.parametrize("name", list(_util.EDGE))
+def test_edge_networks_bit_exact(name, order, kernel):
+    ixs, iy = _util.EDGE[name]
+    nlab = 1 + max(l for ix in ixs for l in ix)
+    nw = (nlab + 63) // 64
+    nw = nw + (nw & 1) if nw > 1 else nw
+    if kernel in ("warp", "pair") and nw not in (1, 2, 4, 6, 8):
+        pytest.skip("no shared-memory layout for this width")
+    if kernel == "pair" and order == "preorder":
+        pytest.skip("two warps per chain is the par-order kernel")
+    net, onet = engine.Network(ixs, iy, nlab), O.Net(ixs, iy, nlab)
+    trees = np.stack([O.random_tree(onet.m, 3, c) for c in range(16)])
+    betas = np.array([0.5, 1.0, 2.0, 4.0], np.float32)
+    t, lab, st = _gpu_sweeps(net, trees, betas, 3, order, 3, 2.0, kernel=kernel)
+    ot, olab, ocnt = O.sweeps(onet, trees, betas, 3, order=order, seed=3, sc_target=2.0)
+    assert (t == ot).all(), f"{(t != ot).any(1).sum()} chains differ"
+    assert (lab[:, :, :onet.nw] == olab).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
+
+
 @pytest.mark.parametrize("name,order", [("grid24", "par"), ("grid24", "preorder"), ("sq46", "par")])
 def test_block_kernel_two_ctas_per_sm(name, order):
     """More chains than SMs: the CTA-per-chain kernel runs two 8-warp CTAs per SM.  A chain's trajectory

@@ -56,6 +56,22 @@ def test_oracle_matches_cpu_ref_live(name, order):
     assert a[2][0] == b[2][0] and a[2][1] == b[2][1]
 
 
+@pytest.mark.parametrize("name", list(_util.EDGE))
+def test_oracle_matches_cpu_ref_on_edge_networks(name, golden):
+    """Small and degenerate networks (three tensors, an empty tensor, disconnected parts, open legs, a
+    star, rings at the packed-word boundaries): the reference's own digests, both orders."""
+    ixs, iy = _util.EDGE[name]
+    nlab = 1 + max(l for ix in ixs for l in ix)
+    net = O.Net(ixs, iy, nlab)
+    trees = np.stack([O.random_tree(net.m, 3, c) for c in range(16)])
+    for order in ("par", "preorder"):
+        exp = [e for e in golden[1]["edge"] if e["instance"] == name and e["order"] == order][0]
+        t, lab, cnt = O.sweeps(net, trees, np.array(exp["betas"], np.float32), exp["niters"], order=order,
+                               seed=exp["seed"], sc_target=exp["sc_target"])
+        assert _util.digest(t, lab) == exp["sha256"], order
+        assert cnt[0] == exp["proposals"] and cnt[1] == exp["accepts"], order
+
+
 def test_oracle_matches_cpu_ref_par_variants(golden):
     """--par-band L and --par-follow (cpu_ref.h:140-175): the reference's own digests."""
     for e in golden[1]["variants"]:
