@@ -60,6 +60,9 @@ def test_argument_errors_are_reported_not_fatal():
     assert rc == 1 and "2..16" in msg
     assert _create(tri, par_band=17)[0] == 1
     assert _create(tri, kernel_hint=3, par_follow=True)[0] == 1
+    big = [[i, (i + 1) % 32769] for i in range(32769)]  # node ids are 16-bit: at most 32768 tensors
+    rc, msg = _create(big)
+    assert rc == 1 and "16-bit" in msg
 
 
 def test_run_reports_errors_through_the_python_api():

@@ -228,6 +228,56 @@ def test_host_exp_mode_equals_oracle_trajectories(name, scheme):
         assert abs(od["tc"] - d["tc"]) < 1e-9 and od["sc"] == d["sc"]
 
 
+def _sat(n, m, seed):
+    rng = np.random.default_rng(seed)
+    return [sorted(int(x) for x in rng.choice(n, 3, replace=False)) for _ in range(m)]
+
+
+@pytest.mark.parametrize("order,sliced", [("par", False), ("preorder", False), ("par", True)])
+def test_large_network_metadata_in_global_memory(order, sliced):
+    """8520 tensors on 2000 labels (the size of the reference's sat2000 fixture): the CTA kernel's per-node
+    metadata does not fit in shared memory, so the children, cost and summary words stay in the record
+    in global memory (kernel code 5); trajectories equal the oracle's, also with a fixed slice set."""
+    ixs = _sat(2000, 8520, 2)
+    net, onet = engine.Network(ixs, [], 2000), O.Net(ixs, [], 2000)
+    trees = np.stack([O.random_tree(onet.m, 5, c) for c in range(4)])
+    betas = CHECK_BETAS[:3]
+    S, sl = None, None
+    if sliced:
+        sl = sorted(int(x) for x in np.random.default_rng(3).choice(2000, 12, replace=False))
+        S = np.zeros(onet.nw, np.uint64)
+        for l in sl:
+            S[l >> 6] |= np.uint64(1) << np.uint64(l & 63)
+    opts = dict(betas=betas, niters=2, nchains=4, sc_target=60.0, order=order, seed=5, init_trees=trees)
+    if sl:
+        opts["init_slices"] = sl
+    s = engine.Session(net, **opts)
+    info = s.info()
+    assert info["kernel"] == 5, info
+    s.run()
+    t, lab = s.chains()
+    st = s.stats()
+    s.close()
+    ot, olab, ocnt = O.sweeps(onet, trees, betas, 2, order=order, seed=5, sc_target=60.0,
+                              S=None if S is None else np.tile(S, (4, 1)))
+    assert (t == ot).all() and (lab[:, :, :onet.nw] == olab).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
+
+
+def test_large_network_slice_moves_end_to_end():
+    """Annealed slice sets on the global-metadata plan, end to end against the oracle's run."""
+    ixs = _sat(2000, 8520, 4)
+    net, onet = engine.Network(ixs, [], 2000), O.Net(ixs, [], 2000)
+    kw = dict(betas=_util.julia_betas(0.01, 2.5, 8.0), niters=2, nchains=8, sc_target=120.0, slicing=True,
+              seed=5, scheme="indep")
+    rc, d = engine.run(net, **kw)
+    orc, od = O.run(onet, **kw)
+    assert rc == 0 and d["valid"] and d["labels_ok"] and d["kernel"] == "block_hbm_gmeta"
+    assert d["tree"] == od["tree"] and d["sliced"] == od["sliced"] and d["n_repair"] == od["n_repair"]
+    assert d["slice_proposals"] == od["slice_proposals"] and d["slice_accepts"] == od["slice_accepts"]
+    assert abs(d["tc"] - od["tc"]) < 1e-9 and d["sc"] == od["sc"]
+
+
 @pytest.mark.parametrize("kernel", ["warp", "pair", "block"])
 @pytest.mark.parametrize("order", ["par", "preorder"])
 @pytest.mark.parametrize("name", list(_util.EDGE))

@@ -1346,6 +1346,7 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
            s->plan.kind == tsa::K_WARP   ? "warp_smem"
            : s->plan.kind == tsa::K_PAIR ? "pair_smem"
            : s->plan.cluster == 2        ? "cta_pair_hbm"
+           : s->plan.gmeta               ? "block_hbm_gmeta"
                                          : "block_hbm");
   res->h2d_bytes = s->h2d;
   res->d2h_bytes = s->d2h;
@@ -1420,7 +1421,9 @@ int tsa_session_info(tsa_session* s, int32_t* v) {
   v[1] = s->L.nint;
   v[2] = s->L.nw;
   v[3] = (int32_t)s->L.rec_bytes;
-  v[4] = s->plan.kind == tsa::K_WARP ? 1 : s->plan.kind == tsa::K_BLOCK ? (s->plan.cluster == 2 ? 4 : 2) : 3;
+  v[4] = s->plan.kind == tsa::K_WARP    ? 1
+         : s->plan.kind == tsa::K_BLOCK ? (s->plan.cluster == 2 ? 4 : s->plan.gmeta ? 5 : 2)
+                                        : 3;
   v[5] = s->plan.warps_per_cta;
   v[6] = s->plan.grid;
   v[7] = (int32_t)s->plan.smem;

@@ -1164,19 +1164,27 @@ struct BlockSmem {
   int nint2;
   // pair: the layout of k_anneal_cluster, which also keeps the leaf chunk summaries in shared memory (its
   // label loads bypass L1; the single-CTA kernel leaves that room to L1, which serves its reloads)
-  __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves, bool pair = false) {
+  // gmeta: the children, cost and summary words are read and written in the chain record in global
+  // memory (networks whose per-node metadata does not fit in shared memory)
+  __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves, bool pair = false,
+                                            bool gmeta = false) {
     BlockSmem b;
     b.nint2 = (int)rnd_up((uint32_t)L.nint, 8);
     const uint32_t n2 = (uint32_t)b.nint2;
     uint32_t o = 1024;  // [0,256) lse, [256,768) exp, [768,1024) block scalars
-    b.off_ch = o;
-    o += 4 * n2;
-    b.off_cz = o;
-    o += 4 * n2;
+    b.off_ch = b.off_cz = b.off_sum = 0;
+    if (!gmeta) {
+      b.off_ch = o;
+      o += 4 * n2;
+      b.off_cz = o;
+      o += 4 * n2;
+    }
     b.off_cz2 = o;
     if (slice_moves > 0) o += 4 * n2;
-    b.off_sum = o;
-    if (L.sums) o += 8 * n2;
+    if (!gmeta) {
+      b.off_sum = o;
+      if (L.sums) o += 8 * n2;
+    }
     b.off_S = rnd_up(o, 16);
     o = b.off_S + rnd_up(8u * (uint32_t)L.nw, 16);
     // pri and wl are adjacent, and so are U and U2: read as two arrays of n2 words they hold the depth
@@ -1996,11 +2004,12 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
   }
 }
 
-template <bool SUMS, int ORDER, bool MODEL>
+// GM: the chain's children, cost and summary words stay in its record in global memory (plan.gmeta)
+template <bool SUMS, int ORDER, bool MODEL, bool GM>
 __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L = a.L;
-  const BlockSmem Bm = BlockSmem::make(L, a.slice_moves);
+  const BlockSmem Bm = BlockSmem::make(L, a.slice_moves, false, GM);
   const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31, warp = tid >> 5;
   const unsigned FULL = 0xFFFFFFFFu;
   float* s_lse = reinterpret_cast<float*>(smem);
@@ -2028,9 +2037,9 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   B.exptab = s_exp;
   B.leaf = a.leaf;
   B.leaf_sum = a.leaf_sum;
-  B.ch = reinterpret_cast<uint32_t*>(smem + Bm.off_ch);
-  B.cz = reinterpret_cast<uint32_t*>(smem + Bm.off_cz);
-  B.sum = reinterpret_cast<uint64_t*>(smem + Bm.off_sum);
+  B.ch = GM ? nullptr : reinterpret_cast<uint32_t*>(smem + Bm.off_ch);  // GM: set per chain
+  B.cz = GM ? nullptr : reinterpret_cast<uint32_t*>(smem + Bm.off_cz);
+  B.sum = GM ? nullptr : reinterpret_cast<uint64_t*>(smem + Bm.off_sum);
   B.S = reinterpret_cast<uint64_t*>(smem + Bm.off_S);
   uint32_t* cz2 = reinterpret_cast<uint32_t*>(smem + Bm.off_cz2);
   uint16_t* pri = reinterpret_cast<uint16_t*>(smem + Bm.off_pri);
@@ -2063,13 +2072,19 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
     const uint32_t* gch = reinterpret_cast<const uint32_t*>(grec + L.off_ch);
     const uint32_t* gcz = reinterpret_cast<const uint32_t*>(grec + L.off_cz);
     const uint64_t* gS = reinterpret_cast<const uint64_t*>(grec + L.off_S);
-    for (int q = tid; q < nint; q += T) {
-      B.ch[q] = gch[q];
-      B.cz[q] = gcz[q];
-    }
-    if (SUMS) {
-      const uint64_t* gs = reinterpret_cast<const uint64_t*>(grec + L.off_sum);
-      for (int q = tid; q < nint; q += T) B.sum[q] = gs[q];
+    if constexpr (GM) {
+      B.ch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
+      B.cz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
+      B.sum = reinterpret_cast<uint64_t*>(grec + L.off_sum);
+    } else {
+      for (int q = tid; q < nint; q += T) {
+        B.ch[q] = gch[q];
+        B.cz[q] = gcz[q];
+      }
+      if (SUMS) {
+        const uint64_t* gs = reinterpret_cast<const uint64_t*>(grec + L.off_sum);
+        for (int q = tid; q < nint; q += T) B.sum[q] = gs[q];
+      }
     }
     for (int q = tid; q < L.nw; q += T) B.S[q] = gS[q];
     __syncthreads();
@@ -2203,13 +2218,15 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
     uint32_t* wch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
     uint32_t* wcz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
     uint64_t* wS = reinterpret_cast<uint64_t*>(grec + L.off_S);
-    for (int q = tid; q < nint; q += T) {
-      wch[q] = B.ch[q];
-      wcz[q] = B.cz[q];
-    }
-    if (SUMS) {
-      uint64_t* ws = reinterpret_cast<uint64_t*>(grec + L.off_sum);
-      for (int q = tid; q < nint; q += T) ws[q] = B.sum[q];
+    if constexpr (!GM) {
+      for (int q = tid; q < nint; q += T) {
+        wch[q] = B.ch[q];
+        wcz[q] = B.cz[q];
+      }
+      if (SUMS) {
+        uint64_t* ws = reinterpret_cast<uint64_t*>(grec + L.off_sum);
+        for (int q = tid; q < nint; q += T) ws[q] = B.sum[q];
+      }
     }
     for (int q = tid; q < L.nw; q += T) wS[q] = B.S[q];
     __syncthreads();
@@ -2478,8 +2495,9 @@ static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaSt
 
 template <bool SUMS, int ORDER>
 static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
-  auto k = a.mode != 0 ? k_anneal_block<SUMS, ORDER, true> : k_anneal_block<SUMS, ORDER, false>;
-  size_t smem = BlockSmem::make(a.L, a.slice_moves).total;
+  auto k = p.gmeta ? (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, true> : k_anneal_block<SUMS, ORDER, false, true>)
+                   : (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, false> : k_anneal_block<SUMS, ORDER, false, false>);
+  size_t smem = BlockSmem::make(a.L, a.slice_moves, false, p.gmeta != 0).total;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   k<<<p.grid, 32 * p.warps_per_cta, smem, st>>>(a);
@@ -2573,7 +2591,13 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   // more than one wave
   if (hint == 1) return cudaErrorNotSupported;
   BlockSmem bs = BlockSmem::make(L, slice_moves);
-  if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
+  plan->gmeta = 0;
+  if (bs.total > (uint32_t)optin) {
+    // the per-node metadata does not fit: keep children, cost and summary words in the record
+    bs = BlockSmem::make(L, slice_moves, false, true);
+    if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
+    plan->gmeta = 1;
+  }
   plan->kind = K_BLOCK;
   plan->warps_per_cta = 16;
   plan->grid = nchains;
@@ -2590,7 +2614,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   plan->cluster = 1;
   // par order with chunk summaries and at most half as many chains as SMs: a pair of CTAs per chain,
   // if every pair can be resident at once
-  const bool pair_ok = L.sums && order == 0 && slice_moves == 0 && !par_follow && !model;
+  const bool pair_ok = L.sums && order == 0 && slice_moves == 0 && !par_follow && !model && !plan->gmeta;
   if (hint == 4 && !pair_ok) return cudaErrorNotSupported;
   if (pair_ok && (hint == 4 || (hint == 0 && 2 * nchains <= nsm))) {
     const int grid = 2 * nchains;

@@ -70,6 +70,7 @@ struct LaunchPlan {
   int grid;
   size_t smem;
   int cluster = 1;           // K_BLOCK: CTAs per chain (2: k_anneal_cluster)
+  int gmeta = 0;             // K_BLOCK: children, cost and summary words stay in the record in global memory
 };
 
 // Host-side entry points (tsa_kernels.cu).
