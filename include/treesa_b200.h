@@ -33,7 +33,9 @@ enum {
   TSA_ERR_UNSUPPORTED = 4, /* option not available in this build */
   TSA_ERR_NOMEM = 5,       /* device or host allocation failed */
   TSA_ERR_TIMEOUT = 6,     /* a bounded device wait ran out (error status from a kernel) */
-  TSA_ERR_COMM = 7         /* NCCL error in a multi-GPU run */
+  TSA_ERR_COMM = 7,        /* NCCL error in a multi-GPU run */
+  TSA_ERR_DEADLINE = 8     /* the run exceeded options.timeout_s (the reference driver's subprocess timeout,
+                              treesa_gpu/driver.py:305) */
 };
 
 enum { TSA_MODE_TC = 0, TSA_MODE_GPU = 1, TSA_MODE_H100 = 2 };
@@ -99,7 +101,9 @@ typedef struct tsa_options {
   int32_t niters2;            /* sweeps per level of stage 2 (<= 0: niters) */
   const float* betas2;        /* NULL: no stage 2 */
   int32_t nbetas2;
-  int32_t reserved[7];
+  float timeout_s;            /* > 0: wall-clock limit of a run's level loop, checked between levels; the run
+                                 then stops with TSA_ERR_DEADLINE (single-GPU runs; 0: no limit) */
+  int32_t reserved[6];
 } tsa_options;
 
 /* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the

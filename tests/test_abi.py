@@ -60,6 +60,8 @@ def test_argument_errors_are_reported_not_fatal():
     assert rc == 1 and "2..16" in msg
     assert _create(tri, par_band=17)[0] == 1
     assert _create(tri, kernel_hint=3, par_follow=True)[0] == 1
+    rc, msg = _create(tri, timeout_s=-1.0)
+    assert rc == 1 and "timeout_s" in msg
     big = [[i, (i + 1) % 32769] for i in range(32769)]  # node ids are 16-bit: at most 32768 tensors
     rc, msg = _create(big)
     assert rc == 1 and "16-bit" in msg

@@ -104,3 +104,15 @@ def test_optimize_edge_networks(name):
     tree, info = tg.optimize(ixs, iy, nchains=64, niters=3, sc_target=10, init="random")
     _check(tree, info, ixs, iy, len(ixs))
 
+
+def test_timeout_stops_the_run_like_the_reference_subprocess():
+    """optimize(timeout=...) stops between levels and raises subprocess.TimeoutExpired, as the reference's
+    subprocess.run(timeout=...) does (treesa_gpu/driver.py:305); the device stays usable."""
+    import subprocess
+    rec = _util.instance("sat100")
+    kw = dict(nchains=512, niters=10, sc_target=20, init="random", betas=[0.01 + 0.05 * i for i in range(300)])
+    with pytest.raises(subprocess.TimeoutExpired):
+        tg.optimize(rec["ixs"], rec["iy"], timeout=1e-4, **kw)
+    tree, info = tg.optimize(rec["ixs"], rec["iy"], timeout=600, **dict(kw, betas=kw["betas"][:20]))
+    assert info["valid"] and info["nlevels"] == 20
+

@@ -19,7 +19,11 @@ SCHEME_NAME = {v: k for k, v in SCHEME.items()}
 ORDER_NAME = {v: k for k, v in ORDER.items()}
 
 ERRORS = {1: "invalid argument", 2: "invalid result tree", 3: "CUDA error", 4: "unsupported option",
-          5: "out of memory", 6: "device wait timed out", 7: "NCCL error"}
+          5: "out of memory", 6: "device wait timed out", 7: "NCCL error", 8: "time limit exceeded"}
+
+
+class DeadlineError(RuntimeError):
+    """A run stopped at its time limit (TSA_ERR_DEADLINE)."""
 
 
 class Instance(C.Structure):
@@ -40,7 +44,8 @@ class Options(C.Structure):
                 ("nccl_id", C.c_void_p), ("verbose", C.c_int32), ("max_levels", C.c_int32),
                 ("exp_mode", C.c_int32), ("kernel_hint", C.c_int32), ("par_follow", C.c_int32),
                 ("par_band", C.c_int32), ("mode2", C.c_int32), ("niters2", C.c_int32),
-                ("betas2", C.POINTER(C.c_float)), ("nbetas2", C.c_int32), ("reserved", C.c_int32 * 7)]
+                ("betas2", C.POINTER(C.c_float)), ("nbetas2", C.c_int32), ("timeout_s", C.c_float),
+                ("reserved", C.c_int32 * 6)]
 
 
 class Result(C.Structure):
@@ -100,7 +105,8 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
                  order="par", seed=1, eval_every=1, slicing=False, slice_moves=1, slice_every=1, max_slices=0,
                  init_slices=(), select_sc=False, init_trees=None, gpu_model=None, h100_model=None, device=0,
                  stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc",
-                 exp_mode="host", kernel_hint=0, par_follow=False, par_band=0, betas2=None, niters2=0, mode2="gpu"):
+                 exp_mode="host", kernel_hint=0, par_follow=False, par_band=0, betas2=None, niters2=0, mode2="gpu",
+                 timeout_s=0.0):
     o = Options()
     o.betas, _ = keep.arr(np.asarray(betas, np.float32), np.float32, C.c_float)
     o.nbetas = len(betas)
@@ -150,6 +156,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
         o.nbetas2 = len(betas2)
         o.niters2 = int(niters2 or 0)
         o.mode2 = MODE[mode2]
+    o.timeout_s = float(timeout_s or 0.0)
     return o
 
 
@@ -229,4 +236,5 @@ def lib():
 def check(rc, err, what):
     if rc != 0:
         msg = err.value.decode(errors="replace") if hasattr(err, "value") else str(err)
-        raise RuntimeError(f"{what} failed ({rc}: {ERRORS.get(rc, 'error')}): {msg}")
+        cls = DeadlineError if rc == 8 else RuntimeError
+        raise cls(f"{what} failed ({rc}: {ERRORS.get(rc, 'error')}): {msg}")

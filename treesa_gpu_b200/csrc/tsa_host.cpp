@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <functional>
 #include <map>
 #include <mutex>
@@ -499,6 +500,7 @@ struct tsa_session {
   int mode0 = 0;     // energy of the first level
   int cur_mode = 0;  // energy of the current level (score() depends on it)
   int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1, exp_device = 0;
+  double timeout_s = 0;  // > 0: wall-clock limit of a run's level loop (single-GPU runs)
   double sc_target = 20, sc_weight = 1, trunc_frac = 0.25;
   uint64_t seed = 1;
   uint32_t key0 = 0, key1 = 0;
@@ -791,6 +793,12 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
   }
   s->par_band = O->order == TSA_ORDER_PAR ? O->par_band : 0;
   s->par_follow = O->order == TSA_ORDER_PAR && O->par_follow ? 1 : 0;
+  if (!(O->timeout_s >= 0.0f) || std::isinf(O->timeout_s)) {
+    set_err(err, errlen, "timeout_s must be a finite number >= 0");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  s->timeout_s = O->timeout_s;
   bool model = false;
   for (int md : s->lmode) model = model || md != TSA_MODE_TC;
   if (O->kernel_hint == 3 && (s->par_band || s->par_follow || model)) {
@@ -1079,11 +1087,22 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     }
     return TSA_OK;
   };
+  // the reference driver's `timeout` (subprocess.run, treesa_gpu/driver.py:305), checked between levels.  A
+  // rank of a multi-GPU run never stops alone: its peers would wait for it in their next collective.
+  auto past_deadline = [&](size_t lev) -> bool {
+    if (s->timeout_s <= 0 || s->world > 1 || now_s() - t0 <= s->timeout_s) return false;
+    set_err(err, errlen, "run stopped at its time limit of %g s before level %zu of %zu", s->timeout_s, lev, nlev);
+    return true;
+  };
   int rc = TSA_OK;
   uint8_t* buf[2] = {s->d_rec, s->d_rec2};
   if (pipelined) {
     long pend = -1;  // evaluated level whose energies are in flight
     for (size_t lev = 0; lev <= nlev && rc == TSA_OK; lev++) {
+      if (lev < nlev && past_deadline(lev)) {
+        rc = TSA_ERR_DEADLINE;
+        break;
+      }
       if (lev < nlev) {
         const int q = (int)(lev & 1);
         if (lev >= 2) {  // the timing events of level lev-2 are reused now
@@ -1148,6 +1167,10 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   } else {
     s->d_cur = s->d_rec;
     for (size_t lev = 0; lev < nlev && rc == TSA_OK; lev++) {
+      if (past_deadline(lev)) {
+        rc = TSA_ERR_DEADLINE;
+        break;
+      }
       if (s->lmode[lev] != s->cur_mode) {
         // stage switch (:1789-1799): the incumbent, rescored in the new energy, stays the best until beaten
         s->cur_mode = s->lmode[lev];

@@ -15,12 +15,13 @@ but "auto"/"par" selects the pre-order sweep), and the par-order variants ``par_
 """
 import heapq
 import math
+import subprocess
 import sys
 import time
 
 import numpy as np
 
-from . import engine, trees
+from . import _abi, engine, trees
 
 DEFAULT_GPU_MODEL = dict(trees.GPU_MODEL)
 DEFAULT_H100_MODEL = dict(trees.H100_MODEL)
@@ -268,12 +269,16 @@ def optimize(ixs, iy, nchains=1024, betas=None, niters=50, sc_target=20.0, sc_we
                 h100_model=[float(h100m[k]) for k in H100_KEYS], device=0 if device is None else int(device),
                 verbose=verbose, rank=rank, world_size=world, nccl_id=nccl_id, stream=stream,
                 par_follow=bool(par_follow), par_band=int(par_band or 0),
-                mode=mode if mode in ("tc", "gpu", "h100") else "tc")
+                mode=mode if mode in ("tc", "gpu", "h100") else "tc",
+                timeout_s=float(timeout) if timeout else 0.0)
     if mode in ("tc+gpu", "tc+h100"):  # stage 2 continues the population in the model energy (driver.py:245-251)
         opts.update(betas2=_betas32(stage2_betas if stage2_betas is not None else julia_betas(1.0, 0.05, 16.0)),
                     niters2=int(stage2_niters or niters), mode2=mode.split("+")[1])
     t0 = time.time()
-    rc, res = engine.run(net, **opts)
+    try:
+        rc, res = engine.run(net, **opts)
+    except _abi.DeadlineError as e:  # the reference's CLI run under subprocess.run(timeout=...)
+        raise subprocess.TimeoutExpired("treesa_gpu_b200.tsa_run", timeout) from e
     wall = time.time() - t0
     if rc != 0:
         raise RuntimeError(f"treesa_gpu_b200 failed ({rc}): final tree invalid or labels mismatch")
