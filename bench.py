@@ -306,7 +306,7 @@ def main():
     bset = 8 * nw64
     nint = rec["m"] - 1
     P, A, V = tot["proposals"], tot["accepts"], tot["visits"]
-    if info["kernel"] in (2, 4, 5) and tot["chunks"] > 0:
+    if info["kernel"] in (2, 4, 5, 6) and tot["chunks"] > 0:
         sum_b = 8 if nw64 >= 32 else 0
         sets = tot["chunks"] * 16 * (6 if W["slicing"] else 5) + P * 4 * sum_b
         alg = (V - P) * 4 + P * 8 + sets + tot["chunks_acc"] * 16 + A * (8 + sum_b)
@@ -321,7 +321,8 @@ def main():
             "traffic": trf, "peak_kind": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                                           else "fallback"),
             "kernel": {1: "k_anneal_warp", 2: "k_anneal_block", 3: "k_anneal_pair", 4: "k_anneal_cluster",
-                       5: "k_anneal_block (global metadata)"}[info["kernel"]],
+                       5: "k_anneal_block (global metadata)", 6: "k_anneal_block (global metadata, full scans)"}[
+                           info["kernel"]],
             "algorithmic_bytes_per_launch": alg_rank / max(1, launches),
             "kernel_visits_per_s": world * W["nchains"] * len(W["betas"]) * W["niters"] * nint * args.steps / KS,
             "kernel_s": KS, "launches_per_step": launches // args.steps}

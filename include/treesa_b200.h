@@ -196,8 +196,8 @@ int tsa_path_costs(const tsa_instance* inst, int32_t norders, const int32_t* ord
 
 /* Layout and plan of a session: info8 = {m, internal nodes, u64 words per label set, record bytes,
  * kernel (1 warp per chain, 2 CTA per chain, 3 two warps per chain, 4 two CTAs per chain, 5 CTA per
- * chain with the children/cost/summary words in global memory), warps per CTA, grid, dynamic shared
- * memory bytes}. */
+ * chain with the children/cost/summary words in global memory, 6 as 5 with every phase scanning all
+ * nodes: the largest networks), warps per CTA, grid, dynamic shared memory bytes}. */
 int tsa_session_info(tsa_session* s, int32_t* info8);
 
 /* Energies of every chain after the last evaluated level (lcost per slice, sc, |S|), for tests. */

@@ -264,6 +264,53 @@ def test_large_network_metadata_in_global_memory(order, sliced):
     assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
 
 
+@pytest.mark.parametrize("nvar,order,sliced", [(7000, "par", False), (7000, "preorder", False), (7000, "par", True),
+                                               (1500, "par", False)])
+def test_largest_networks_scan_all_nodes(nvar, order, sliced):
+    """30000 tensors (the reference handles up to 32767): even the global-metadata layout's unvisited
+    lists do not fit, so every phase scans all nodes (kernel code 6), with (7000 labels) and without
+    (1500 labels) chunk summaries; trajectories equal the oracle's."""
+    m = 30000
+    ixs = _sat(nvar, m, 6)
+    net, onet = engine.Network(ixs, [], nvar), O.Net(ixs, [], nvar)
+    trees = np.stack([O.random_tree(onet.m, 5, c) for c in range(4)])
+    betas = CHECK_BETAS[:2]
+    S, sl = None, None
+    if sliced:
+        sl = sorted(int(x) for x in np.random.default_rng(3).choice(nvar, 12, replace=False))
+        S = np.zeros(onet.nw, np.uint64)
+        for l in sl:
+            S[l >> 6] |= np.uint64(1) << np.uint64(l & 63)
+    opts = dict(betas=betas, niters=2, nchains=4, sc_target=200.0, order=order, seed=5, init_trees=trees)
+    if sl:
+        opts["init_slices"] = sl
+    s = engine.Session(net, **opts)
+    info = s.info()
+    assert info["kernel"] == 6, info
+    s.run()
+    t, lab = s.chains()
+    st = s.stats()
+    s.close()
+    ot, olab, ocnt = O.sweeps(onet, trees, betas, 2, order=order, seed=5, sc_target=200.0,
+                              S=None if S is None else np.tile(S, (4, 1)))
+    assert (t == ot).all() and (lab[:, :, :onet.nw] == olab).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
+
+
+def test_largest_network_slice_moves_end_to_end():
+    """Annealed slice sets on the full-scan plan (the slice-move cost scratch lives in global memory)."""
+    ixs = _sat(1500, 30000, 7)
+    net, onet = engine.Network(ixs, [], 1500), O.Net(ixs, [], 1500)
+    kw = dict(betas=_util.julia_betas(0.01, 4.0, 8.0), niters=2, nchains=4, sc_target=400.0, slicing=True,
+              seed=5, scheme="indep")
+    rc, d = engine.run(net, **kw)
+    orc, od = O.run(onet, **kw)
+    assert rc == 0 and d["valid"] and d["labels_ok"] and d["kernel"] == "block_hbm_gmeta_scan"
+    assert d["tree"] == od["tree"] and d["sliced"] == od["sliced"] and d["n_repair"] == od["n_repair"]
+    assert d["slice_proposals"] == od["slice_proposals"] and d["slice_accepts"] == od["slice_accepts"]
+    assert abs(d["tc"] - od["tc"]) < 1e-9 and d["sc"] == od["sc"]
+
+
 def test_large_network_slice_moves_end_to_end():
     """Annealed slice sets on the global-metadata plan, end to end against the oracle's run."""
     ixs = _sat(2000, 8520, 4)

@@ -516,6 +516,7 @@ struct tsa_session {
   float *d_lse = nullptr, *d_lc = nullptr;
   int *d_sc = nullptr, *d_ns = nullptr, *d_anc = nullptr, *d_err = nullptr;
   unsigned long long* d_stats = nullptr;
+  uint32_t* d_scratch = nullptr;  // [nchains][nint] slice-move cost scratch (plan gmeta 2 only)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   cudaEvent_t evk[4] = {nullptr, nullptr, nullptr, nullptr};  // kernel start/end, two level parities
   cudaEvent_t eve[2] = {nullptr, nullptr};                    // energies of a level on the host
@@ -547,6 +548,7 @@ struct tsa_session {
     if (st) cudaStreamSynchronize(st);  // nothing in flight touches the blocks handed back to the cache
     if (cst) cudaStreamSynchronize(cst);
     for (void* p : {(void*)d_rec, (void*)d_rec2, (void*)d_init, (void*)d_leaf, (void*)d_leaf_sum, (void*)d_lse,
+                    (void*)d_scratch,
                     (void*)d_lc, (void*)d_sc, (void*)d_ns, (void*)d_anc, (void*)d_err, (void*)d_stats, (void*)h_lc,
                     (void*)h_sc, (void*)h_ns, (void*)h_best})
       pool_free(p);
@@ -592,12 +594,14 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
   }
   bool model = false;
   for (int md : s->lmode) model = model || md != TSA_MODE_TC;
-  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, s->order, s->slice_moves, s->par_follow,
+  if (tsa::plan_sweeps(s->L, s->nchains, s->device, O->kernel_hint, s->order, s->slice_moves, s->par_band, s->par_follow,
                        model ? 1 : 0, &s->plan) !=
       cudaSuccess) {
     set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
     return TSA_ERR_UNSUPPORTED;
   }
+  if (s->plan.gmeta == 2 && s->slice_moves > 0)  // cost words of proposed slice sets, per chain
+    CKR(pool_alloc(0, &s->d_scratch, (size_t)s->nchains * s->L.nint * sizeof(uint32_t)));
   const size_t recb = (size_t)s->L.rec_bytes * s->nchains;
   CKR(pool_alloc(0, &s->d_rec, recb));
   CKR(pool_alloc(0, &s->d_init, recb));
@@ -941,6 +945,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.err = s->d_err;
   a.lse_tab = s->d_lse;
   a.leaf_sum = s->d_leaf_sum;
+  a.scratch = s->d_scratch;
   s->best.resize(rb);
   // host side of one evaluated level: best tracking, trace, population step (returns the ancestors)
   auto process = [&](size_t lev, const float* glc, const int* gsc, const int* gns, int* improved) {
@@ -1369,6 +1374,7 @@ int tsa_session_result(tsa_session* s, tsa_result* res, char* err, size_t errlen
            s->plan.kind == tsa::K_WARP   ? "warp_smem"
            : s->plan.kind == tsa::K_PAIR ? "pair_smem"
            : s->plan.cluster == 2        ? "cta_pair_hbm"
+           : s->plan.gmeta == 2          ? "block_hbm_gmeta_scan"
            : s->plan.gmeta               ? "block_hbm_gmeta"
                                          : "block_hbm");
   res->h2d_bytes = s->h2d;
@@ -1445,7 +1451,7 @@ int tsa_session_info(tsa_session* s, int32_t* v) {
   v[2] = s->L.nw;
   v[3] = (int32_t)s->L.rec_bytes;
   v[4] = s->plan.kind == tsa::K_WARP    ? 1
-         : s->plan.kind == tsa::K_BLOCK ? (s->plan.cluster == 2 ? 4 : s->plan.gmeta ? 5 : 2)
+         : s->plan.kind == tsa::K_BLOCK ? (s->plan.cluster == 2 ? 4 : s->plan.gmeta ? 4 + s->plan.gmeta : 2)
                                         : 3;
   v[5] = s->plan.warps_per_cta;
   v[6] = s->plan.grid;

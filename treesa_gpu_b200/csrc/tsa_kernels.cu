@@ -1164,10 +1164,11 @@ struct BlockSmem {
   int nint2;
   // pair: the layout of k_anneal_cluster, which also keeps the leaf chunk summaries in shared memory (its
   // label loads bypass L1; the single-CTA kernel leaves that room to L1, which serves its reloads)
-  // gmeta: the children, cost and summary words are read and written in the chain record in global
-  // memory (networks whose per-node metadata does not fit in shared memory)
+  // gmeta 1: the children, cost and summary words are read and written in the chain record in global
+  // memory (networks whose per-node metadata does not fit in shared memory); gmeta 2: also no unvisited
+  // lists, no flat-phase tables and no slice-move scratch in shared memory (the largest networks)
   __host__ __device__ static BlockSmem make(const Layout& L, int slice_moves, bool pair = false,
-                                            bool gmeta = false) {
+                                            int gmeta = 0) {
     BlockSmem b;
     b.nint2 = (int)rnd_up((uint32_t)L.nint, 8);
     const uint32_t n2 = (uint32_t)b.nint2;
@@ -1180,7 +1181,7 @@ struct BlockSmem {
       o += 4 * n2;
     }
     b.off_cz2 = o;
-    if (slice_moves > 0) o += 4 * n2;
+    if (slice_moves > 0 && gmeta < 2) o += 4 * n2;
     if (!gmeta) {
       b.off_sum = o;
       if (L.sums) o += 8 * n2;
@@ -1195,11 +1196,14 @@ struct BlockSmem {
     o += 2 * n2;
     b.off_wl = o;
     o += 2 * n2;
-    b.off_U = o;
-    o += 2 * n2;
-    b.off_U2 = o;
-    o += 2 * n2;
-    if (L.sums) {
+    b.off_U = b.off_U2 = 0;
+    if (gmeta < 2) {
+      b.off_U = o;
+      o += 2 * n2;
+      b.off_U2 = o;
+      o += 2 * n2;
+    }
+    if (L.sums && gmeta < 2) {
       o = rnd_up(o, 16);
       b.off_ninfo = o;
       o += 8 * kFlatBatch;
@@ -1614,7 +1618,9 @@ __device__ void slice_step_block(const BlkCtx& B, const SweepArgs& a, uint32_t* 
 // entries per round with all their shared-memory loads issued together (a missing neighbour reads the
 // node's own key, which blocks nothing), and a warp reserves its places for the whole round with one
 // atomic per list.
-template <int R>
+// LIST = false: no lists; every node [0, nU) is an entry, the visited ones (pri 0) skipped, and no kept
+// list is written (U and U2 unused).
+template <int R, bool LIST = true>
 __device__ __forceinline__ void phase_scan(const uint16_t* U, int nU, uint16_t* wl, uint16_t* U2, int* ctr,
                                            const uint16_t* pri, const uint16_t* par, const uint32_t* ch, int m) {
   const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31;
@@ -1625,8 +1631,13 @@ __device__ __forceinline__ void phase_scan(const uint16_t* U, int nU, uint16_t* 
 #pragma unroll
     for (int r = 0; r < R; r++) {
       const int j = base + r * T + tid;
-      valid[r] = j < nU;
-      q[r] = valid[r] ? (int)U[j] : 0;
+      if (LIST) {
+        valid[r] = j < nU;
+        q[r] = valid[r] ? (int)U[j] : 0;
+      } else {
+        q[r] = j < nU ? j : 0;
+        valid[r] = j < nU && pri[q[r]] != 0;
+      }
     }
 #pragma unroll
     for (int r = 0; r < R; r++) {
@@ -1653,14 +1664,14 @@ __device__ __forceinline__ void phase_scan(const uint16_t* U, int nU, uint16_t* 
     int pa = 0, pk = 0;
     if (lane == 0) {
       if (ta) pa = atomicAdd(&ctr[0], ta);
-      if (tk) pk = atomicAdd(&ctr[1], tk);
+      if (LIST && tk) pk = atomicAdd(&ctr[1], tk);
     }
     pa = __shfl_sync(FULL, pa, 0);
     pk = __shfl_sync(FULL, pk, 0);
 #pragma unroll
     for (int r = 0; r < R; r++) {
       if (act[r]) wl[pa + __popc(ba[r] & lt)] = (uint16_t)q[r];
-      if (valid[r] && !act[r]) U2[pk + __popc(bk[r] & lt)] = (uint16_t)q[r];
+      if (LIST && valid[r] && !act[r]) U2[pk + __popc(bk[r] & lt)] = (uint16_t)q[r];
       pa += __popc(ba[r]);
       pk += __popc(bk[r]);
     }
@@ -2004,8 +2015,10 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
   }
 }
 
-// GM: the chain's children, cost and summary words stay in its record in global memory (plan.gmeta)
-template <bool SUMS, int ORDER, bool MODEL, bool GM>
+// GM (plan.gmeta): 1 the chain's children, cost and summary words stay in its record in global memory;
+// 2 also every phase scans all nodes (no unvisited lists), the slice-move scratch is a.scratch, and the
+// phase visits nodes with G lanes each (tc mode, no band / follow-up visits: the plan checks)
+template <bool SUMS, int ORDER, bool MODEL, int GM>
 __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Layout L = a.L;
@@ -2041,12 +2054,12 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   B.cz = GM ? nullptr : reinterpret_cast<uint32_t*>(smem + Bm.off_cz);
   B.sum = GM ? nullptr : reinterpret_cast<uint64_t*>(smem + Bm.off_sum);
   B.S = reinterpret_cast<uint64_t*>(smem + Bm.off_S);
-  uint32_t* cz2 = reinterpret_cast<uint32_t*>(smem + Bm.off_cz2);
+  uint32_t* cz2 = GM == 2 ? nullptr : reinterpret_cast<uint32_t*>(smem + Bm.off_cz2);  // GM 2: per chain
   uint16_t* pri = reinterpret_cast<uint16_t*>(smem + Bm.off_pri);
   uint16_t* par = reinterpret_cast<uint16_t*>(smem + Bm.off_par);
   uint16_t* wl = reinterpret_cast<uint16_t*>(smem + Bm.off_wl);
-  uint16_t* Ua = reinterpret_cast<uint16_t*>(smem + Bm.off_U);
-  uint16_t* Ub = reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
+  uint16_t* Ua = GM == 2 ? nullptr : reinterpret_cast<uint16_t*>(smem + Bm.off_U);
+  uint16_t* Ub = GM == 2 ? nullptr : reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
   float* costs = reinterpret_cast<float*>(Ua);  // model modes: node costs, while the U lists are free
   const int m = L.m, nint = L.nint;
   FlatTabs F;
@@ -2072,10 +2085,11 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
     const uint32_t* gch = reinterpret_cast<const uint32_t*>(grec + L.off_ch);
     const uint32_t* gcz = reinterpret_cast<const uint32_t*>(grec + L.off_cz);
     const uint64_t* gS = reinterpret_cast<const uint64_t*>(grec + L.off_S);
-    if constexpr (GM) {
+    if constexpr (GM != 0) {
       B.ch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
       B.cz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
       B.sum = reinterpret_cast<uint64_t*>(grec + L.off_sum);
+      if constexpr (GM == 2) cz2 = a.scratch ? a.scratch + (size_t)c * nint : nullptr;
     } else {
       for (int q = tid; q < nint; q += T) {
         B.ch[q] = gch[q];
@@ -2104,7 +2118,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
       if (ORDER == 0) {
         const uint32_t hs = sweep_hash(sw, hc);
-        if (a.par_band > 0) {
+        if (GM != 2 && a.par_band > 0) {
           // depths at the start of the sweep in (pri, wl) and (U, U2) read as word arrays
           uint32_t* U32 = reinterpret_cast<uint32_t*>(Ua);
           block_depths(par, m, nint, reinterpret_cast<uint32_t*>(pri), U32);
@@ -2115,12 +2129,12 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
         } else {
           for (int q = tid; q < nint; q += T) {
             pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
-            Ua[q] = (uint16_t)q;
+            if (GM != 2) Ua[q] = (uint16_t)q;
           }
         }
         uint16_t *U = Ua, *U2 = Ub;
         int nU = nint;
-        const bool follow = a.par_follow != 0;
+        const bool follow = GM != 2 && a.par_follow != 0;
         const int max_phases = follow ? 2 * nint : nint;
         // the scan counters alternate between sh[0..1] (even phases) and sh[2..3] (odd phases): a phase
         // clears the next phase's pair behind its own scan barrier, so no barrier is spent on clearing
@@ -2128,7 +2142,10 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
         __syncthreads();
         for (int guard = 0; guard <= max_phases; guard++) {
           int* const ctr = sh + 2 * (guard & 1);
-          phase_scan<4>(U, nU, wl, U2, ctr, pri, par, B.ch, m);
+          if constexpr (GM == 2)
+            phase_scan<4, false>(nullptr, nint, wl, nullptr, ctr, pri, par, B.ch, m);
+          else
+            phase_scan<4>(U, nU, wl, U2, ctr, pri, par, B.ch, m);
           __syncthreads();
           const int nk = ctr[0];
           nU = ctr[1];
@@ -2141,7 +2158,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
           // re-armed pivots (par_follow) are appended to U after the nU kept nodes, counted on in ctr[1]
           const FollowCtx fctx{pri, U, &ctr[1], hs};
           const FollowCtx* fol = follow ? &fctx : nullptr;
-          if constexpr (SUMS && !MODEL) {
+          if constexpr (SUMS && !MODEL && GM != 2) {
             par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{}, fol);
           } else {
             const int G = pick_group(nk, T);
@@ -2218,7 +2235,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
     uint32_t* wch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
     uint32_t* wcz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
     uint64_t* wS = reinterpret_cast<uint64_t*>(grec + L.off_S);
-    if constexpr (!GM) {
+    if constexpr (GM == 0) {
       for (int q = tid; q < nint; q += T) {
         wch[q] = B.ch[q];
         wcz[q] = B.cz[q];
@@ -2495,9 +2512,11 @@ static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaSt
 
 template <bool SUMS, int ORDER>
 static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
-  auto k = p.gmeta ? (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, true> : k_anneal_block<SUMS, ORDER, false, true>)
-                   : (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, false> : k_anneal_block<SUMS, ORDER, false, false>);
-  size_t smem = BlockSmem::make(a.L, a.slice_moves, false, p.gmeta != 0).total;
+  auto k = p.gmeta == 2 ? k_anneal_block<SUMS, ORDER, false, 2>  // tc only (the plan)
+            : p.gmeta   ? (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, 1> : k_anneal_block<SUMS, ORDER, false, 1>)
+                        : (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, 0> : k_anneal_block<SUMS, ORDER, false, 0>);
+  if (p.gmeta == 2 && (a.mode != 0 || (a.slice_moves > 0 && !a.scratch))) return cudaErrorInvalidValue;
+  size_t smem = BlockSmem::make(a.L, a.slice_moves, false, p.gmeta).total;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   k<<<p.grid, 32 * p.warps_per_cta, smem, st>>>(a);
@@ -2542,7 +2561,7 @@ static int cluster_capacity(size_t smem, int grid) {
   return n;
 }
 
-cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves, int par_band,
                         int par_follow, int model, LaunchPlan* plan) {
   int nsm = 0, optin = 0;
   cudaError_t e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
@@ -2594,9 +2613,16 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
   plan->gmeta = 0;
   if (bs.total > (uint32_t)optin) {
     // the per-node metadata does not fit: keep children, cost and summary words in the record
-    bs = BlockSmem::make(L, slice_moves, false, true);
-    if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
+    bs = BlockSmem::make(L, slice_moves, false, 1);
     plan->gmeta = 1;
+    if (bs.total > (uint32_t)optin) {
+      // the largest networks: 6 bytes a node in shared memory, every phase scans all nodes (tc mode,
+      // no band priorities or follow-up visits)
+      if (model || par_band || par_follow) return cudaErrorNotSupported;
+      bs = BlockSmem::make(L, slice_moves, false, 2);
+      if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
+      plan->gmeta = 2;
+    }
   }
   plan->kind = K_BLOCK;
   plan->warps_per_cta = 16;

@@ -59,6 +59,7 @@ struct SweepArgs {
   int par_follow;            // par order: re-visit the pivot child of an accepted first visit
   int mode;                  // energy of this launch: 0 tc, 1 gpu model, 2 h100 model
   ModelParams mp;
+  uint32_t* scratch;         // [nchains][nint] cost words of a proposed slice set (plan gmeta 2 with slice moves)
 };
 
 // Kernel family chosen by the host for a layout.
@@ -70,14 +71,16 @@ struct LaunchPlan {
   int grid;
   size_t smem;
   int cluster = 1;           // K_BLOCK: CTAs per chain (2: k_anneal_cluster)
-  int gmeta = 0;             // K_BLOCK: children, cost and summary words stay in the record in global memory
+  int gmeta = 0;             // K_BLOCK: 1 children, cost and summary words stay in the record in global
+                             // memory; 2 also no unvisited lists (every phase scans all nodes) and the
+                             // slice-move cost scratch in global memory (the largest networks)
 };
 
 // Host-side entry points (tsa_kernels.cu).
 // hint: 0 auto, 1 one warp per chain, 2 one CTA per chain (label sets in HBM), 3 two warps per chain,
 // 4 a pair of CTAs per chain (par order with chunk summaries, no slice moves)
 // model: some level of the run uses an energy mode other than tc
-cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves,
+cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int order, int slice_moves, int par_band,
                         int par_follow, int model, LaunchPlan* plan);
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
