@@ -14,6 +14,9 @@ value: all ranks' visits / max-over-ranks device time of K steps, chains residen
 e2e:   the same metric through the C ABI (tsa_run) from host buffers: host chain init, upload, anneal,
        download and finalize inside the timed region.
 --impl reference: the reference's own CPU path (csrc/cpu_ref.h built into oracle/_ref) on all host cores.
+--impl reference_gpu: the reference's own CLI binary (csrc/treesa_gpu.cu compiled unchanged for sm_100a into
+       oracle/_ref/treesa_gpu_ref by `make -C oracle refgpu`) on the same workload and start trees, timed
+       by its own kernel_s (value) and by the wall time of the process (e2e).
 """
 import argparse
 import json
@@ -92,6 +95,69 @@ def start_trees(rec, seed=1, config="c2"):
         return engine.tree_words(driver.dict_to_children(driver.greedy_tree(rec["ixs"], rec["iy"]), m))[None, :]
     so = spectral.spectral_orders(rec["ixs"], rec["iy"], k=4, seed=seed)
     return np.stack([engine.tree_words(driver.dict_to_children(spectral.path_tree(o), m)) for _, _, o in so])
+
+
+REF_GPU = os.path.join(ROOT, "oracle", "_ref", "treesa_gpu_ref")
+
+
+def reference_gpu_run(W, trees, workdir, device):
+    """One run of the reference's own CLI binary on the workload (its instance, multi-tree and betas file
+    formats, csrc/treesa_gpu.cu:1035-1097 and :1305-1336): (its kernel seconds, process wall seconds,
+    its JSON result)."""
+    rec = W["rec"]
+    inst, tree, betas, out = (os.path.join(workdir, f) for f in ("inst.txt", "trees.txt", "betas.txt", "out.json"))
+    with open(inst, "w") as f:
+        f.write(f"{rec['m']} {rec['nlab']}\n")
+        for ix in rec["ixs"]:
+            f.write(" ".join(str(x) for x in [len(ix)] + list(ix)) + "\n")
+        f.write(" ".join(str(x) for x in [len(rec["iy"])] + list(rec["iy"])) + "\n")
+    with open(tree, "w") as f:
+        for t in np.atleast_2d(trees):
+            for w in t:
+                f.write(f"{int(w) & 0xFFFF} {int(w) >> 16}\n")
+    with open(betas, "w") as f:
+        f.write("\n".join(repr(float(b)) for b in W["betas"]) + "\n")
+    cmd = [REF_GPU, "-i", inst, "--tree", tree, "--nchains", str(W["nchains"]), "--niters", str(W["niters"]),
+           "--betas", "file:" + betas, "--mode", "tc", "--sc-target", str(W["sc_target"]), "--scheme", W["scheme"],
+           "--order", W["order"], "--seed", str(W["seed"]), "--out", out, "--quiet"]
+    if W["slicing"]:
+        cmd.append("--slicing")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(device))
+    t0 = time.time()
+    p = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=1800)
+    wall = time.time() - t0
+    if p.returncode not in (0, 2):
+        raise RuntimeError(f"reference binary failed ({p.returncode}): {p.stderr[-2000:]}")
+    with open(out) as f:
+        res = json.load(f)
+    return float(res["kernel_s"]), wall, res
+
+
+def reference_gpu_arm(W, args, device):
+    import tempfile
+    if not os.path.exists(REF_GPU):
+        print(json.dumps({"impl": "reference_gpu", "unavailable": "oracle/_ref/treesa_gpu_ref not built "
+                          "(make -C oracle refgpu where the reference sources are)"}), flush=True)
+        return 0
+    trees = start_trees(W["rec"], config=W["config"])
+    ks, ws = [], []
+    with tempfile.TemporaryDirectory() as d:
+        for _ in range(args.warmup):
+            reference_gpu_run(W, trees, d, device)
+        for _ in range(args.steps):
+            k, w, res = reference_gpu_run(W, trees, d, device)
+            ks.append(k)
+            ws.append(w)
+    vps = visits_per_step(W, 1)
+    k, w = statistics.median(ks), statistics.median(ws)
+    line = {"metric": METRIC, "value": vps / k, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * k, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u32", "data": "synthetic", "config": config_dict(W, 1),
+            "impl": "reference_gpu", "reference_kernel": res.get("kernel"),
+            "e2e": {"value": vps / w, "unit": UNIT, "note": "wall time of the reference's CLI process"},
+            "best_tc": res.get("tc"), "best_sc": res.get("sc"), "valid": res.get("valid")}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def visits_per_step(W, world):
@@ -194,7 +260,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_gpu"])
     ap.add_argument("--chains", type=int, default=0, help="chains per GPU (default: the config's)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
@@ -230,6 +296,11 @@ def main():
                 "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
+
+    if args.impl == "reference_gpu":
+        if rank != 0:
+            return 0
+        return reference_gpu_arm(W, args, local)
 
     import torch
     torch.cuda.set_device(local)
