@@ -845,23 +845,9 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
           __syncwarp();
           uint32_t cw = 0;
           if (lane < k) cw = visit<NW, false, ChainCounters, MODEL>(X_, lab, ch, cz, NM, par, v, sw, chain, cnt);
-          // internal children with two leaf children are visited here and now (an empty visit)
+          // internal children become ready (one with two leaf children takes an empty visit next step)
           bool c1 = lane < k && (int)(cw & 0xFFFFu) >= m;
           bool c2 = lane < k && (int)(cw >> 16) >= m;
-          if (c1) {
-            uint32_t g = ch[(cw & 0xFFFFu) - m];
-            if ((int)(g & 0xFFFFu) < m && (int)(g >> 16) < m) {
-              c1 = false;
-              cnt.visits++;
-            }
-          }
-          if (c2) {
-            uint32_t g = ch[(cw >> 16) - m];
-            if ((int)(g & 0xFFFFu) < m && (int)(g >> 16) < m) {
-              c2 = false;
-              cnt.visits++;
-            }
-          }
           unsigned b1 = __ballot_sync(FULL, c1), b2 = __ballot_sync(FULL, c2);
           int pos = b0 + __popc(b1 & lt) + __popc(b2 & lt);
           if (c2) wl[pos++] = (uint16_t)((cw >> 16) - (uint32_t)m);
