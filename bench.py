@@ -77,7 +77,7 @@ def workload(nchains, config="c2"):
 
 
 def config_dict(W, world):
-    return {"workload": CONFIGS[W["config"]].format(n=W["nchains"]), "config": W["config"],
+    return {"workload": CONFIGS[W["config"]].format(n=W["nchains"]), "config": W["config"], "order": W["order"],
             "m": W["rec"]["m"], "labels": W["rec"]["nlab"], "chains_per_gpu": W["nchains"],
             "levels": len(W["betas"]), "sweeps_per_level": W["niters"],
             "parallelism": f"chains sharded over {world} GPU(s)",
@@ -266,6 +266,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--levels", type=int, default=0, help="first L beta levels only (profiling runs)")
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS), help="BASELINE config (default c2)")
+    ap.add_argument("--order", default="", choices=["", "par", "preorder"],
+                    help="sweep order instead of the config's (a side measurement, not a BASELINE config)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -274,6 +276,8 @@ def main():
     W = workload(nch, args.config)
     if args.levels > 0:
         W["betas"] = W["betas"][:args.levels]
+    if args.order:
+        W["order"] = args.order
 
     if args.impl == "reference":
         if rank != 0:
