@@ -297,6 +297,29 @@ def test_largest_networks_scan_all_nodes(nvar, order, sliced):
     assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
 
 
+@pytest.mark.parametrize("band,follow,mode", [(4, False, "tc"), (0, True, "tc"), (0, False, "h100"),
+                                               (3, True, "gpu")])
+def test_largest_networks_variants_and_energy_modes(band, follow, mode):
+    """The full-scan plan with band priorities, follow-up visits and the model energies (their per-node
+    scratch in global memory): trajectories equal the oracle's."""
+    ixs = _sat(1500, 30000, 8)
+    net, onet = engine.Network(ixs, [], 1500), O.Net(ixs, [], 1500)
+    trees = np.stack([O.random_tree(onet.m, 5, c) for c in range(4)])
+    betas = CHECK_BETAS[:2]
+    s = engine.Session(net, betas=betas, niters=2, nchains=4, sc_target=200.0, order="par", seed=5,
+                       init_trees=trees, par_band=band, par_follow=follow, mode=mode)
+    info = s.info()
+    assert info["kernel"] == 6, info
+    s.run()
+    t, lab = s.chains()
+    st = s.stats()
+    s.close()
+    ot, olab, ocnt = O.sweeps(onet, trees, betas, 2, order="par", seed=5, sc_target=200.0, par_band=band,
+                              par_follow=follow, mode=mode)
+    assert (t == ot).all() and (lab[:, :, :onet.nw] == olab).all()
+    assert st["proposals"] == ocnt[0] and st["accepts"] == ocnt[1]
+
+
 def test_largest_network_slice_moves_end_to_end():
     """Annealed slice sets on the full-scan plan (the slice-move cost scratch lives in global memory)."""
     ixs = _sat(1500, 30000, 7)

@@ -600,8 +600,9 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
     set_err(err, errlen, "no sweep kernel for this layout (%d internal nodes, %d label words)", s->L.nint, s->L.nw);
     return TSA_ERR_UNSUPPORTED;
   }
-  if (s->plan.gmeta == 2 && s->slice_moves > 0)  // cost words of proposed slice sets, per chain
-    CKR(pool_alloc(0, &s->d_scratch, (size_t)s->nchains * s->L.nint * sizeof(uint32_t)));
+  if (s->plan.gmeta == 2 && (s->slice_moves > 0 || model || s->par_band > 0))
+    // per chain: 2 words a node (slice-move costs and model-mode costs, or the band depths)
+    CKR(pool_alloc(0, &s->d_scratch, (size_t)s->nchains * 2 * s->L.nint * sizeof(uint32_t)));
   const size_t recb = (size_t)s->L.rec_bytes * s->nchains;
   CKR(pool_alloc(0, &s->d_rec, recb));
   CKR(pool_alloc(0, &s->d_init, recb));

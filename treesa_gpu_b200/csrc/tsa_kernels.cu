@@ -1303,7 +1303,7 @@ struct FollowCtx {
 __device__ __forceinline__ void follow_rearm(const FollowCtx* f, int Pn, int m) {
   if (f && f->pri[Pn - m] == 0) {
     f->pri[Pn - m] = (uint16_t)follow_pri((uint32_t)Pn, f->hs);
-    f->U[atomicAdd(f->nU, 1)] = (uint16_t)(Pn - m);
+    if (f->U) f->U[atomicAdd(f->nU, 1)] = (uint16_t)(Pn - m);  // no list: the full scan finds it
   }
 }
 
@@ -2002,8 +2002,9 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
 }
 
 // GM (plan.gmeta): 1 the chain's children, cost and summary words stay in its record in global memory;
-// 2 also every phase scans all nodes (no unvisited lists), the slice-move scratch is a.scratch, and the
-// phase visits nodes with G lanes each (tc mode, no band / follow-up visits: the plan checks)
+// 2 also every phase scans all nodes (no unvisited lists), visits them with G lanes each, and the
+// per-node scratch (slice-move costs, model-mode costs, band depths) is the chain's 2 nint words of
+// a.scratch
 template <bool SUMS, int ORDER, bool MODEL, int GM>
 __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -2046,7 +2047,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
   uint16_t* wl = reinterpret_cast<uint16_t*>(smem + Bm.off_wl);
   uint16_t* Ua = GM == 2 ? nullptr : reinterpret_cast<uint16_t*>(smem + Bm.off_U);
   uint16_t* Ub = GM == 2 ? nullptr : reinterpret_cast<uint16_t*>(smem + Bm.off_U2);
-  float* costs = reinterpret_cast<float*>(Ua);  // model modes: node costs, while the U lists are free
+  float* costs = reinterpret_cast<float*>(Ua);  // model modes: node costs, while the U lists are free (GM 2: per chain)
   const int m = L.m, nint = L.nint;
   FlatTabs F;
   F.info = reinterpret_cast<uint2*>(smem + Bm.off_ninfo);
@@ -2075,7 +2076,10 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
       B.ch = reinterpret_cast<uint32_t*>(grec + L.off_ch);
       B.cz = reinterpret_cast<uint32_t*>(grec + L.off_cz);
       B.sum = reinterpret_cast<uint64_t*>(grec + L.off_sum);
-      if constexpr (GM == 2) cz2 = a.scratch ? a.scratch + (size_t)c * nint : nullptr;
+      if constexpr (GM == 2) {
+        cz2 = a.scratch ? a.scratch + (size_t)c * 2 * nint : nullptr;
+        costs = a.scratch ? reinterpret_cast<float*>(cz2 + nint) : nullptr;
+      }
     } else {
       for (int q = tid; q < nint; q += T) {
         B.ch[q] = gch[q];
@@ -2104,14 +2108,17 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
       const uint32_t sw = a.sweep0 + (uint32_t)s;
       if (ORDER == 0) {
         const uint32_t hs = sweep_hash(sw, hc);
-        if (GM != 2 && a.par_band > 0) {
-          // depths at the start of the sweep in (pri, wl) and (U, U2) read as word arrays
-          uint32_t* U32 = reinterpret_cast<uint32_t*>(Ua);
-          block_depths(par, m, nint, reinterpret_cast<uint32_t*>(pri), U32);
+        if (a.par_band > 0) {
+          // depths at the start of the sweep in (pri, wl) and (U, U2) read as word arrays (GM 2: in the
+          // chain's scratch words)
+          uint32_t* A0 = GM == 2 ? cz2 : reinterpret_cast<uint32_t*>(pri);
+          uint32_t* U32 = GM == 2 ? cz2 + nint : reinterpret_cast<uint32_t*>(Ua);
+          block_depths(par, m, nint, A0, U32);
           for (int q = tid; q < nint; q += T)
             pri[q] = (uint16_t)band_pri(node_pri((uint32_t)(m + q), hs), (int)(U32[q] >> 16), a.par_band);
           __syncthreads();
-          for (int q = tid; q < nint; q += T) Ua[q] = (uint16_t)q;
+          if (GM != 2)
+            for (int q = tid; q < nint; q += T) Ua[q] = (uint16_t)q;
         } else {
           for (int q = tid; q < nint; q += T) {
             pri[q] = (uint16_t)node_pri((uint32_t)(m + q), hs);
@@ -2120,7 +2127,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
         }
         uint16_t *U = Ua, *U2 = Ub;
         int nU = nint;
-        const bool follow = GM != 2 && a.par_follow != 0;
+        const bool follow = a.par_follow != 0;
         const int max_phases = follow ? 2 * nint : nint;
         // the scan counters alternate between sh[0..1] (even phases) and sh[2..3] (odd phases): a phase
         // clears the next phase's pair behind its own scan barrier, so no barrier is spent on clearing
@@ -2142,7 +2149,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
           if (nk == 0) break;
           if (tid == 0) cnt.steps++;
           // re-armed pivots (par_follow) are appended to U after the nU kept nodes, counted on in ctr[1]
-          const FollowCtx fctx{pri, U, &ctr[1], hs};
+          const FollowCtx fctx{pri, GM == 2 ? nullptr : U, &ctr[1], hs};
           const FollowCtx* fol = follow ? &fctx : nullptr;
           if constexpr (SUMS && !MODEL && GM != 2) {
             par_phase_flat<true, 1>(B, F, wl, pri, par, nk, sw, chain, cnt, PeerArrays{}, fol);
@@ -2498,10 +2505,10 @@ static cudaError_t launch_warp_o(const SweepArgs& a, const LaunchPlan& p, cudaSt
 
 template <bool SUMS, int ORDER>
 static cudaError_t launch_block_t(const SweepArgs& a, const LaunchPlan& p, cudaStream_t st) {
-  auto k = p.gmeta == 2 ? k_anneal_block<SUMS, ORDER, false, 2>  // tc only (the plan)
+  auto k = p.gmeta == 2 ? (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, 2> : k_anneal_block<SUMS, ORDER, false, 2>)
             : p.gmeta   ? (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, 1> : k_anneal_block<SUMS, ORDER, false, 1>)
                         : (a.mode != 0 ? k_anneal_block<SUMS, ORDER, true, 0> : k_anneal_block<SUMS, ORDER, false, 0>);
-  if (p.gmeta == 2 && (a.mode != 0 || (a.slice_moves > 0 && !a.scratch))) return cudaErrorInvalidValue;
+  if (p.gmeta == 2 && !a.scratch && (a.slice_moves > 0 || a.mode != 0 || a.par_band > 0)) return cudaErrorInvalidValue;
   size_t smem = BlockSmem::make(a.L, a.slice_moves, false, p.gmeta).total;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -2602,9 +2609,7 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
     bs = BlockSmem::make(L, slice_moves, false, 1);
     plan->gmeta = 1;
     if (bs.total > (uint32_t)optin) {
-      // the largest networks: 6 bytes a node in shared memory, every phase scans all nodes (tc mode,
-      // no band priorities or follow-up visits)
-      if (model || par_band || par_follow) return cudaErrorNotSupported;
+      // the largest networks: 6 bytes a node in shared memory, every phase scans all nodes
       bs = BlockSmem::make(L, slice_moves, false, 2);
       if (bs.total > (uint32_t)optin) return cudaErrorNotSupported;
       plan->gmeta = 2;

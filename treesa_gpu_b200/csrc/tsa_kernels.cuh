@@ -59,7 +59,7 @@ struct SweepArgs {
   int par_follow;            // par order: re-visit the pivot child of an accepted first visit
   int mode;                  // energy of this launch: 0 tc, 1 gpu model, 2 h100 model
   ModelParams mp;
-  uint32_t* scratch;         // [nchains][nint] cost words of a proposed slice set (plan gmeta 2 with slice moves)
+  uint32_t* scratch;         // plan gmeta 2: [nchains][2 nint] words: slice-move and model-mode costs, band depths
 };
 
 // Kernel family chosen by the host for a layout.
