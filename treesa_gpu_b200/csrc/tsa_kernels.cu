@@ -1287,6 +1287,7 @@ __device__ __forceinline__ void for_chunks(uint64_t u, int nchunks, int G, int t
       k++;
     }
   } else {
+#pragma unroll 4
     for (int c = t; c < nchunks; c += G) f(c);
   }
 }
