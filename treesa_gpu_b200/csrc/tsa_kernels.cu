@@ -138,6 +138,35 @@ __device__ __forceinline__ void stset(uint64_t* p, const Set<NW>& s) {
   }
 }
 
+// The same loads and stores through 32-bit shared-memory addresses (the warp kernels keep the chain and
+// the leaf table in shared memory): one select and one multiply-add a set instead of 64-bit pointers.
+// The memory clobber keeps them in order with the kernels' other shared-memory accesses.
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+template <int NW>
+__device__ __forceinline__ Set<NW> ldset_s(uint32_t a) {
+  Set<NW> s;
+  if constexpr (NW % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < NW / 2; i++)
+      asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(s.w[2 * i]), "=l"(s.w[2 * i + 1]) : "r"(a + 16u * i) : "memory");
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW; i++) asm volatile("ld.shared.u64 %0, [%1];" : "=l"(s.w[i]) : "r"(a + 8u * i) : "memory");
+  }
+  return s;
+}
+template <int NW>
+__device__ __forceinline__ void stset_s(uint32_t a, const Set<NW>& s) {
+  if constexpr (NW % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < NW / 2; i++)
+      asm volatile("st.shared.v2.u64 [%0], {%1, %2};" ::"r"(a + 16u * i), "l"(s.w[2 * i]), "l"(s.w[2 * i + 1]) : "memory");
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW; i++) asm volatile("st.shared.u64 [%0], %1;" ::"r"(a + 8u * i), "l"(s.w[i]) : "memory");
+  }
+}
+
 // Per-launch constants kept in registers / shared memory of a warp.
 struct WarpCtx {
   int m, nint;
@@ -279,10 +308,11 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
   uint32_t chp = ch[p.Pn - m];
   p.Mn = slotM ? (int)(chp >> 16) : (int)(chp & 0xFFFFu);
   int Kn = slotM ? (int)(chp & 0xFFFFu) : (int)(chp >> 16);
-  const uint64_t* pO = p.On >= m ? lab + (size_t)(p.On - m) * NW : X_.leaf + (size_t)p.On * NW;
-  const uint64_t* pK = Kn >= m ? lab + (size_t)(Kn - m) * NW : X_.leaf + (size_t)Kn * NW;
-  const uint64_t* pM = p.Mn >= m ? lab + (size_t)(p.Mn - m) * NW : X_.leaf + (size_t)p.Mn * NW;
-  Set<NW> D = ldset<NW>(lab + (size_t)p.i * NW), O = ldset<NW>(pO), K = ldset<NW>(pK), M = ldset<NW>(pM);
+  // node n's set: internal at labA + n * 8NW (wrapping arithmetic), leaf at leafA + n * 8NW
+  const uint32_t labA = saddr(lab) - (uint32_t)(m * NW * 8), leafA = saddr(X_.leaf);
+  auto sa = [&](int n) { return (n >= m ? labA : leafA) + (uint32_t)n * (uint32_t)(NW * 8); };
+  Set<NW> D = ldset_s<NW>(labA + (uint32_t)v * (uint32_t)(NW * 8)), O = ldset_s<NW>(sa(p.On)),
+          K = ldset_s<NW>(sa(Kn)), M = ldset_s<NW>(sa(p.Mn));
   int sx = 0, k2 = 0, k3 = 0;
   C4 c[4] = {};
 #pragma unroll
@@ -295,7 +325,7 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
     k3 += __popcll(xm & M.w[w] & ~D.w[w]);
   }
   if constexpr (MODEL) {
-    const Set<NW> Pset = ldset<NW>(lab + (size_t)(p.Pn - m) * NW);
+    const Set<NW> Pset = ldset_s<NW>(labA + (uint32_t)p.Pn * (uint32_t)(NW * 8));
 #pragma unroll
     for (int w = 0; w < NW; w++) {
       const uint64_t nm = NM.w[w], k = K.w[w] & nm, mm = M.w[w] & nm, pp = Pset.w[w] & nm, o = O.w[w] & nm,
@@ -329,7 +359,7 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
 template <int NW, bool PAR>
 __device__ __forceinline__ void apply(const Prop<NW>& p, int m, uint64_t* lab, uint32_t* ch, uint32_t* cz,
                                       uint16_t* par) {
-  stset<NW>(lab + (size_t)(p.Pn - m) * NW, p.X);
+  stset_s<NW>(saddr(lab) + (uint32_t)(p.Pn - m) * (uint32_t)(NW * 8), p.X);
   cz[p.Pn - m] = ((uint32_t)p.cP1 << 16) | (uint32_t)p.sx;
   cz[p.i] = ((uint32_t)p.cV1 << 16) | (uint32_t)p.sd;
   ch[p.Pn - m] = p.nchp;
