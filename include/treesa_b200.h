@@ -132,6 +132,9 @@ typedef struct tsa_result {
 
 /* TSA_ABI_VERSION of the loaded library. */
 int tsa_abi_version(void);
+/* sizes[0..2] = sizeof(tsa_instance), sizeof(tsa_options), sizeof(tsa_result): lets a binding (ctypes,
+ * cgo, ...) check its struct mirrors against this build. */
+int tsa_abi_sizes(int32_t* sizes);
 
 /* One annealing run (reference: the whole CLI run, Runner<W>::run_anneal, :1756-1923).
  * Replaces driver.py:215-314.  Thread-safe; concurrent calls on different devices run in parallel. */

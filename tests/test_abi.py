@@ -25,6 +25,15 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert "tsa_run" in names and "tsa_session_create" in names
     for n in names:
         assert hasattr(L, n), f"{n} declared in include/treesa_b200.h but not exported"
+    assert L.tsa_release_cached_memory() == 0  # an empty block cache is released without a device
+
+
+def test_ctypes_structs_match_the_library():
+    """The ctypes mirrors of tsa_instance / tsa_options / tsa_result have the library's sizes."""
+    sizes = (C.c_int32 * 3)()
+    assert _abi.lib().tsa_abi_sizes(sizes) == 0
+    assert list(sizes) == [C.sizeof(_abi.Instance), C.sizeof(_abi.Options), C.sizeof(_abi.Result)]
+    assert _abi.Options.timeout_s.offset == 220 and _abi.Options.reserved.offset == 224
 
 
 def _create(ixs, iy=(), nlab=None, **kw):

@@ -70,7 +70,7 @@ TRACE_COLS = ["t", "level", "beta", "best_lcost_per_slice", "best_sc", "mean_E",
 EXPORTS = ["tsa_abi_version", "tsa_run", "tsa_result_free", "tsa_session_create", "tsa_session_run",
            "tsa_session_result", "tsa_session_reset", "tsa_session_destroy", "tsa_session_stats",
            "tsa_session_energies", "tsa_session_chains", "tsa_nccl_unique_id", "tsa_session_info",
-           "tsa_resample", "tsa_resample_noalloc", "tsa_release_cached_memory"]
+           "tsa_resample", "tsa_resample_noalloc", "tsa_release_cached_memory", "tsa_abi_sizes"]
 
 
 class Packed:
@@ -216,6 +216,7 @@ def lib():
                                      C.c_size_t]
     L.tsa_nccl_unique_id.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
     L.tsa_release_cached_memory.argtypes = []
+    L.tsa_abi_sizes.argtypes = [C.POINTER(C.c_int32)]
     L.tsa_session_info.argtypes = [C.c_void_p, C.POINTER(C.c_int32)]
     L.tsa_resample.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int32, C.c_uint32, C.c_void_p, C.c_char_p,
                                C.c_size_t]

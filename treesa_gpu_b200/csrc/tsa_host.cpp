@@ -720,6 +720,14 @@ extern "C" {
 
 int tsa_abi_version(void) { return TSA_ABI_VERSION; }
 
+int tsa_abi_sizes(int32_t* sizes) {
+  if (!sizes) return TSA_ERR_ARG;
+  sizes[0] = (int32_t)sizeof(tsa_instance);
+  sizes[1] = (int32_t)sizeof(tsa_options);
+  sizes[2] = (int32_t)sizeof(tsa_result);
+  return TSA_OK;
+}
+
 int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_session** out, char* err, size_t errlen) {
   if (!out || !O) {
     set_err(err, errlen, "null argument");
