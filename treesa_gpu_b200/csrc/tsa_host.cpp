@@ -548,9 +548,8 @@ struct tsa_session {
     if (st) cudaStreamSynchronize(st);  // nothing in flight touches the blocks handed back to the cache
     if (cst) cudaStreamSynchronize(cst);
     for (void* p : {(void*)d_rec, (void*)d_rec2, (void*)d_init, (void*)d_leaf, (void*)d_leaf_sum, (void*)d_lse,
-                    (void*)d_scratch,
-                    (void*)d_lc, (void*)d_sc, (void*)d_ns, (void*)d_anc, (void*)d_err, (void*)d_stats, (void*)h_lc,
-                    (void*)h_sc, (void*)h_ns, (void*)h_best})
+                    (void*)d_scratch, (void*)d_lc, (void*)d_sc, (void*)d_ns, (void*)d_anc, (void*)d_err,
+                    (void*)d_stats, (void*)h_lc, (void*)h_sc, (void*)h_ns, (void*)h_best})
       pool_free(p);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
