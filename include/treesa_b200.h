@@ -176,8 +176,8 @@ int tsa_resample(void* records, const int32_t* anc, int32_t nchains, uint32_t re
                  size_t errlen);
 
 /* tsa_resample without any allocation, for callers that cannot allocate device memory when they
- * resample: a host thread capturing a CUDA graph, a process whose device memory belongs to its own fixed
- * pool, or a loop where cudaMalloc/cudaFree would synchronize the device.  Same arguments and result as
+ * resample: a process whose device memory belongs to its own fixed pool, or a loop where
+ * cudaMalloc/cudaFree would synchronize the device.  Same arguments and result as
  * tsa_resample; the scratch is a static device array built into the library (64 MiB of records and
  * 65536 ancestor slots, held by every GPU that loads it until exit), so at most 65536 chains and 64 MiB
  * of records; larger populations are rejected with TSA_ERR_ARG.  The first call on a device (with that

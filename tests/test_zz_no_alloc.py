@@ -1,6 +1,6 @@
 """tsa_resample_noalloc: the population resample for callers that cannot allocate device memory when they
-call it (a thread capturing a CUDA graph, a process with its own fixed device pool, a loop where
-cudaMalloc would synchronize).  Called through the C ABI, its records must equal those of tsa_resample,
+call it (a process whose device memory belongs to its own fixed pool, a loop where cudaMalloc would
+synchronize the device).  Called through the C ABI, its records must equal those of tsa_resample,
 the allocating entry point, on two calls in a row (the second with other ancestors, over the scratch the
 first call left behind).  The data are bytes, so the comparison is exact.  This file sorts last so that a
 run stopping at its first failure has run every other test; it also passes alone in a fresh process."""

@@ -2,9 +2,8 @@
 //
 // tsa_resample gathers every chain record's ancestor through a scratch copy of the population that it
 // allocates with cudaMalloc for the call.  Some callers cannot allocate device memory at that point: a
-// host thread that is capturing work into a CUDA graph (a cudaMalloc there fails or breaks the capture),
-// a serving process whose device memory is owned by its own fixed pool after start-up, or a latency-bound
-// loop where cudaMalloc/cudaFree would synchronize the device.  tsa_resample_noalloc does the same gather
+// serving process whose device memory is owned by its own fixed pool after start-up, or a latency-bound
+// loop where cudaMalloc/cudaFree would synchronize the device and stall the work queued around it.  tsa_resample_noalloc does the same gather
 // through scratch space that the library reserves once, in this file: a static device array of
 // kScratchBytes bytes of records and kMaxChains ancestor slots, held by every GPU that loads this code
 // until the process exits.
