@@ -15,7 +15,7 @@ e2e:   the same metric through the C ABI (tsa_run) from host buffers: host chain
        download and finalize inside the timed region.
 --impl reference: the reference's own CPU path (csrc/cpu_ref.h built into oracle/_ref) on all host cores.
 --impl reference_gpu: the reference's own CLI binary (csrc/treesa_gpu.cu compiled unchanged for sm_100a into
-       oracle/_ref/treesa_gpu_ref by `make -C oracle refgpu`) on the same workload and start trees, timed
+       oracle/_ref/treesa_gpu_ref by `make -C oracle refgpu REF=<reference>/csrc`) on the same workload and start trees, timed
        by its own kernel_s (value) and by the wall time of the process (e2e).
 """
 import argparse
@@ -31,49 +31,10 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from workloads import CONFIGS, DEFAULT_CHAINS, start_trees, workload  # noqa: E402
+
 METRIC = "node visits/s"
 UNIT = "visits/s"
-
-
-CONFIGS = {
-    "c1": "C1: random 3-SAT n=60 m=256 (sat60), path start in clause order, order preorder, sc_target 20, "
-          "64 chains, betas 0.01:0.05:15 x 10 sweeps",
-    "c2": "C2: random 3-SAT n=100 m=426 (sat100), spectral start, order par, tc/sc sc_target 20, best-of-N, "
-          "{n} chains per GPU, betas 0.01:0.05:15 x 10 sweeps",
-    "c3": "C3: random 3-regular n=2000 (configuration model, seed 1), 3000 edge + 2000 vertex tensors, "
-          "spectral start, order par, population annealing (resampling every beta), {n} chains per GPU, "
-          "betas 0.01:0.05:15 x 10 sweeps",
-    "c4": "C4: 64x64 open lattice (4096 tensors, 8064 labels), row-major path start, order par, best-of-N, "
-          "{n} chains per GPU x 20 sweeps, betas 0.01:0.05:15",
-    "c5": "C5: grid 3-SAT L=24 alpha 4.26 (2454 clauses, 576 vars, seed 1), slicing sc_target 30, greedy start, "
-          "truncation selection, {n} chains per GPU, betas 0.01:0.05:15 x 10 sweeps",
-}
-DEFAULT_CHAINS = {"c1": 64, "c2": 4096, "c3": 1024, "c4": 72, "c5": 576}
-
-
-def workload(nchains, config="c2"):
-    """The BASELINE configuration as (instance, schedule, options); start trees built by start_trees."""
-    from tests import _instances, _util
-    betas = _util.julia_betas(0.01, 0.05, 15.0)
-    base = dict(config=config, nchains=nchains, betas=betas, niters=10, sc_target=20.0, order="par",
-                scheme="indep", seed=1, slicing=False)
-    if config in ("c1", "c2"):
-        rec = _util.instance("sat60" if config == "c1" else "sat100")
-        base.update(rec=rec)
-        if config == "c1":
-            base.update(order="preorder")
-    else:
-        ixs, iy = {"c3": lambda: _instances.reg3_dual(2000, 1), "c4": lambda: _instances.sq(64),
-                   "c5": lambda: _instances.grid_ksat(24, 4.26, 1)}[config]()
-        labs = {l for ix in ixs for l in ix}
-        base.update(rec=dict(ixs=ixs, iy=iy, m=len(ixs), nlab=1 + max(labs)))
-        if config == "c3":
-            base.update(scheme="pa")
-        elif config == "c4":
-            base.update(niters=20)
-        else:
-            base.update(scheme="trunc", slicing=True, sc_target=30.0)
-    return base
 
 
 def config_dict(W, world):
@@ -82,19 +43,6 @@ def config_dict(W, world):
             "levels": len(W["betas"]), "sweeps_per_level": W["niters"],
             "parallelism": f"chains sharded over {world} GPU(s)",
             "l2": "flushed between steps (256 MiB write)"}
-
-
-def start_trees(rec, seed=1, config="c2"):
-    """C1: path tree in clause order; C4: row-major path; C5: greedy tree; C2/C3: 4 spectral path trees."""
-    from tests import _instances
-    from treesa_gpu_b200 import driver, engine, spectral
-    m = rec["m"]
-    if config in ("c1", "c4"):
-        return _instances.path_words(list(range(m)), m)[None, :]
-    if config == "c5":
-        return engine.tree_words(driver.dict_to_children(driver.greedy_tree(rec["ixs"], rec["iy"]), m))[None, :]
-    so = spectral.spectral_orders(rec["ixs"], rec["iy"], k=4, seed=seed)
-    return np.stack([engine.tree_words(driver.dict_to_children(spectral.path_tree(o), m)) for _, _, o in so])
 
 
 REF_GPU = os.path.join(ROOT, "oracle", "_ref", "treesa_gpu_ref")
@@ -137,7 +85,7 @@ def reference_gpu_arm(W, args, device):
     import tempfile
     if not os.path.exists(REF_GPU):
         print(json.dumps({"impl": "reference_gpu", "unavailable": "oracle/_ref/treesa_gpu_ref not built "
-                          "(make -C oracle refgpu where the reference sources are)"}), flush=True)
+                          "(make -C oracle refgpu REF=<reference>/csrc where the reference sources are)"}), flush=True)
         return 0
     trees = start_trees(W["rec"], config=W["config"])
     ks, ws = [], []
@@ -167,6 +115,19 @@ def visits_per_step(W, world):
 # ------------------------------------------------------------------------------------------------
 # CPU: the reference's own cpu_ref.h (oracle/_ref), all host threads, bounded sample
 # ------------------------------------------------------------------------------------------------
+def cpu_model():
+    """The host CPU's model name (/proc/cpuinfo), or the platform's processor string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def cpu_reference_rate(W, trees, target_s=12.0):
     import oracle as O
     rec = W["rec"]
@@ -190,7 +151,7 @@ def cpu_reference_rate(W, trees, target_s=12.0):
     v1, s1 = run(2)
     nlev = int(max(2, min(len(betas), 2 * target_s / max(s1, 1e-3))))
     v, s = run(nlev)
-    return dict(value=v / s, unit=UNIT, cores=threads, kind=kind,
+    return dict(value=v / s, unit=UNIT, cores=threads, cpu_model=cpu_model(), kind=kind,
                 sample=f"{nch} chains x first {nlev} of {len(betas)} levels x {W['niters']} sweeps "
                        f"({W['config']}, order {W['order']}), {s:.1f} s")
 
@@ -245,13 +206,19 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def ncu_traffic(config="c2"):
-    """DRAM bytes per launch of the sweep kernel from the committed ncu summary (None if absent)."""
+def ncu_record(config="c2"):
+    """The committed ncu summary of the config's sweep kernel (profiles/<config>_sweep_ncu.json): DRAM bytes
+    per launch and, for the shared-memory kernels, warp instructions per node visit ({} if absent)."""
     p = os.path.join(ROOT, "profiles", f"{config}_sweep_ncu.json")
     if os.path.exists(p):
         with open(p) as f:
-            return json.load(f).get("dram_bytes_per_launch")
-    return None
+            return json.load(f)
+    return {}
+
+
+def sm_count(device):
+    import torch
+    return torch.cuda.get_device_properties(device).multi_processor_count
 
 
 # ------------------------------------------------------------------------------------------------
@@ -264,7 +231,8 @@ def main():
     ap.add_argument("--chains", type=int, default=0, help="chains per GPU (default: the config's)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--levels", type=int, default=0, help="first L beta levels only (profiling runs)")
+    ap.add_argument("--levels", default="", help="profiling runs only: the first L beta levels (L), or levels "
+                                                   "a..b-1 of the schedule (a:b)")
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS), help="BASELINE config (default c2)")
     ap.add_argument("--order", default="", choices=["", "par", "preorder"],
                     help="sweep order instead of the config's (a side measurement, not a BASELINE config)")
@@ -274,8 +242,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     nch = args.chains if args.chains > 0 else DEFAULT_CHAINS[args.config]
     W = workload(nch, args.config)
-    if args.levels > 0:
-        W["betas"] = W["betas"][:args.levels]
+    if args.levels:
+        a, _, b = args.levels.rpartition(":")
+        W["betas"] = W["betas"][int(a or 0):int(b)]
     if args.order:
         W["order"] = args.order
 
@@ -391,16 +360,30 @@ def main():
     alg_rank = alg / world  # the counters are summed over ranks, the kernel time is the slowest rank's
     peak, peak_kind = measured_peak()
     achieved = alg_rank / KS / 1e9
-    trf = ncu_traffic(W["config"])
-    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": trf, "peak_kind": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                                          else "fallback"),
-            "kernel": {1: "k_anneal_warp", 2: "k_anneal_block", 3: "k_anneal_pair", 4: "k_anneal_cluster",
-                       5: "k_anneal_block (global metadata)", 6: "k_anneal_block (global metadata, full scans)"}[
-                           info["kernel"]],
-            "algorithmic_bytes_per_launch": alg_rank / max(1, launches),
-            "kernel_visits_per_s": world * W["nchains"] * len(W["betas"]) * W["niters"] * nint * args.steps / KS,
-            "kernel_s": KS, "launches_per_step": launches // args.steps}
+    ncu = ncu_record(W["config"])
+    trf = ncu.get("dram_bytes_per_launch")
+    kvps = world * W["nchains"] * len(W["betas"]) * W["niters"] * nint * args.steps / KS
+    hbm = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+           "traffic": trf, "peak_kind": (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                                         else "fallback")}
+    kname = {1: "k_anneal_warp", 2: "k_anneal_block", 3: "k_anneal_pair", 4: "k_anneal_cluster",
+             5: "k_anneal_block (global metadata)", 6: "k_anneal_block (global metadata, full scans)"}[info["kernel"]]
+    extra = {"kernel": kname, "algorithmic_bytes_per_launch": alg_rank / max(1, launches),
+             "kernel_visits_per_s": kvps, "kernel_s": KS, "launches_per_step": launches // args.steps}
+    ipv = ncu.get("warp_inst_per_visit")
+    if info["kernel"] in (1, 3) and ipv:
+        # The chain lives in shared memory (HBM sees one record read and write per launch): the roof is
+        # instruction issue.  achieved = warp instructions per node visit (ncu, committed) x the visits/s
+        # measured here; peak = 4 schedulers x SMs x the SM clock sampled during the timed region.
+        mhz = clocks["sm_mhz"] if clocks else 1965.0
+        ipk = 4.0 * sm_count(local) * mhz * 1e6 / 1e9
+        ach = ipv * (kvps / world) / 1e9
+        roof = {"bound": "issue", "achieved": ach, "peak": ipk, "unit": "G warp-instructions/s", "frac": ach / ipk,
+                "traffic": trf, "peak_kind": f"4 issue slots x {sm_count(local)} SMs x {mhz:.0f} MHz (sampled)",
+                "warp_inst_per_visit": ipv, "hbm": hbm}
+    else:
+        roof = dict(hbm)
+    roof.update(extra)
 
     # e2e through the C ABI with host buffers
     e2e_t, h2d, d2h = 0.0, 0, 0

@@ -41,6 +41,7 @@ enum {
 enum { TSA_MODE_TC = 0, TSA_MODE_GPU = 1, TSA_MODE_H100 = 2 };
 enum { TSA_SCHEME_INDEP = 0, TSA_SCHEME_PA = 1, TSA_SCHEME_TRUNC = 2 };
 enum { TSA_ORDER_PAR = 0, TSA_ORDER_PREORDER = 1 };
+enum { TSA_DEBUG_ARM_ONLY = 1 };
 
 /* Tensor network: ixs in CSR form (driver.write_instance, driver.py:70-77; read_instance,
  * csrc/treesa_gpu.cu:1035-1073).  Labels inside one tensor must be distinct. */
@@ -103,7 +104,13 @@ typedef struct tsa_options {
   int32_t nbetas2;
   float timeout_s;            /* > 0: wall-clock limit of a run's level loop, checked between levels; the run
                                  then stops with TSA_ERR_DEADLINE (single-GPU runs; 0: no limit) */
-  int32_t reserved[6];
+  int32_t wait_log2;          /* a bounded device wait (a chain's staging copy into shared memory) gives up
+                                 after 2^wait_log2 SM cycles and the call returns TSA_ERR_TIMEOUT; 0: 31 (about
+                                 a second at 1.9 GHz); 10..31 */
+  int32_t debug_flags;        /* tests only, 0 otherwise.  TSA_DEBUG_ARM_ONLY: the warp kernels arm their
+                                 staging barrier for a chain's record but issue no copy, so the bounded wait
+                                 runs out with nothing in flight (exercises the TSA_ERR_TIMEOUT path) */
+  int32_t reserved[4];
 } tsa_options;
 
 /* Result (library-owned buffers, freed by tsa_result_free).  Field names are the JSON keys of the

@@ -24,9 +24,25 @@ _ORC = None
 _REF = None
 
 
+def reference_csrc():
+    """The reference's csrc/ directory: $TREESA_REFERENCE/csrc, else BASELINE.json's reference_path; None
+    where neither names an existing source tree (the GPU box keeps the prebuilt _ref/ files)."""
+    import json
+    root = os.environ.get("TREESA_REFERENCE")
+    if not root:
+        p = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+        if os.path.exists(p):
+            with open(p) as f:
+                root = json.load(f).get("reference_path")
+    if root and os.path.exists(os.path.join(root, "csrc", "cpu_ref.h")):
+        return os.path.join(root, "csrc")
+    return None
+
+
 def build(quiet=True):
     """Compile the oracle (and the reference harness where the reference sources exist)."""
-    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    ref = reference_csrc()
+    out = subprocess.run(["make", "-C", HERE] + ([f"REF={ref}"] if ref else []), capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout[-3000:] + out.stderr[-3000:])
     if not quiet:

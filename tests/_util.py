@@ -27,10 +27,7 @@ def words(tree):
     return (t[:, 0] | (t[:, 1] << 16)).astype(np.uint32)
 
 
-def julia_betas(a=0.01, st=0.05, e=15.0):
-    """Julia range a:st:e as float32 (driver.julia_betas, then the binary's float conversion)."""
-    n = int(np.floor((e - a) / st + 1e-9)) + 1
-    return np.array([a + i * st for i in range(n)], np.float32)
+from workloads import julia_betas  # noqa: E402,F401  (Julia range a:st:e as float32)
 
 
 def start_trees(rec, nchains, seed):

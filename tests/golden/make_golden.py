@@ -1,7 +1,10 @@
-"""Generate the golden fixtures of the test suite from the reference (run in a container where the
-reference tree is mounted; the fixtures are committed and the GPU box never reads the reference).
+"""Generate the golden fixtures of the test suite from the reference (run where the reference's source
+tree exists; the fixtures are committed and the GPU box never reads the reference).
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py [REFERENCE_ROOT] [--baseline]
+
+REFERENCE_ROOT defaults to $TREESA_REFERENCE, else BASELINE.json's "reference_path".  --baseline only
+(re)computes section (g) and keeps the rest of expected.json.
 
 Writes
   instances.json  -- instances of the reference's tests/data (binary instance format, read_instance
@@ -23,7 +26,13 @@ Writes
                      (f) small and degenerate networks (tests/_util.EDGE: three tensors, an empty
                      tensor, disconnected parts, open legs, a star, rings at the packed-word
                      boundaries), 16 random start trees, betas 0.5/1/2/4 x 3 sweeps, sc_target 2, seed 3,
-                     both orders.
+                     both orders;
+                     (g) the BASELINE workloads (workloads.py) on their own schedules through cpu_ref.h:
+                     C1 whole (64 chains x 300 levels x 10 sweeps, pre-order); C2 whole (4096 chains x
+                     300 x 10, par, from its 4 spectral start trees, stored here), as one digest per
+                     block of 64 chains; C3 / C4 / C5 at full size on a few chains over three levels of
+                     the schedule (its first, middle and last beta) x the config's sweeps, C5 with a
+                     fixed slice set.
 """
 import hashlib
 import json
@@ -73,6 +82,67 @@ def digest(trees, labels):
     h.update(np.ascontiguousarray(trees, np.uint32).tobytes())
     h.update(np.ascontiguousarray(labels, np.uint64).tobytes())
     return h.hexdigest()
+
+
+def baseline(ref_unused=None):
+    """Section (g): the BASELINE workloads through the reference's cpu_ref.h (all host threads)."""
+    import time
+
+    import oracle as O
+    import workloads as WL
+    out = []
+    lv = WL.julia_betas(0.01, 0.05, 15.0)
+    three = [float(lv[0]), float(lv[len(lv) // 2]), float(lv[-1])]
+
+    def run(cfg, trees, betas, niters, order, sc_target, c0=0, S=None, block=0):
+        ixs, iy, nlab = WL.instance(cfg)
+        net = O.Net(ixs, iy, nlab)
+        t0 = time.time()
+        t, l, cnt, _ = O.ref_sweeps(net, trees, np.asarray(betas, np.float32), niters, order=order, seed=1,
+                                    sc_target=sc_target, c0=c0, S=S)
+        e = dict(config=cfg, order=order, niters=niters, nbetas=len(betas), seed=1, sc_target=sc_target, c0=c0,
+                 nchains=len(trees), proposals=int(cnt[0]), accepts=int(cnt[1]))
+        if block:
+            e["block"] = block
+            e["sha256_blocks"] = [digest(t[b:b + block], l[b:b + block]) for b in range(0, len(trees), block)]
+        else:
+            e["sha256"] = digest(t, l)
+        print(cfg, len(trees), "chains", f"{time.time() - t0:.1f} s", flush=True)
+        return e
+
+    # C1 whole: path start in clause order
+    W1 = WL.workload(64, "c1")
+    t1 = WL.start_trees(W1["rec"], "c1")
+    e = run("c1", np.repeat(t1, 64, 0), lv, 10, "preorder", 20.0)
+    e.update(betas="0.01:0.05:15")
+    out.append(e)
+    # C2 whole: 4096 chains, chain c from spectral tree c % 4
+    W2 = WL.workload(4096, "c2")
+    t2 = WL.start_trees(W2["rec"], "c2")
+    e = run("c2", np.stack([t2[c % len(t2)] for c in range(4096)]), lv, 10, "par", 20.0, block=64)
+    e.update(betas="0.01:0.05:15", start_trees=[[int(x) for x in t] for t in t2])
+    out.append(e)
+    # C3 / C4 / C5 at full size: a few chains, first / middle / last beta
+    for cfg, nch, niters in (("c3", 8, 10), ("c4", 4, 20), ("c5", 8, 10)):
+        W = WL.workload(nch, cfg)
+        st = WL.start_trees(W["rec"], cfg)
+        trees = np.stack([st[c % len(st)] for c in range(nch)])
+        S = None
+        sl = None
+        if cfg == "c5":
+            nlab = W["rec"]["nlab"]
+            sl = sorted(int(x) for x in np.random.default_rng(5).choice(nlab, 6, replace=False))
+            nw = (nlab + 63) // 64
+            S1 = np.zeros(nw, np.uint64)
+            for q in sl:
+                S1[q >> 6] |= np.uint64(1) << np.uint64(q & 63)
+            S = np.tile(S1, (nch, 1))
+        e = run(cfg, trees, three, niters, "par", W["sc_target"], S=S)
+        e.update(betas=three, start_trees=[[int(x) for x in t] for t in st])
+        if sl:
+            e["slices"] = sl
+        out.append(e)
+    return out
 
 
 def main(ref):
@@ -159,11 +229,32 @@ def main(ref):
         if r.get("init") == "sweep" and r.get("niters") == 20 and r["instance"] in ("sq32", "sq48", "sq64"):
             large.append(dict(instance=r["instance"], nchains=r["nchains"], niters=r["niters"], beta0=r["beta0"],
                               tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
+    exp = dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes, edge=edge)
+    exp["baseline"] = baseline(ref)
     with open(os.path.join(HERE, "expected.json"), "w") as f:
-        json.dump(dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes, edge=edge), f, indent=1)
+        json.dump(exp, f, indent=1)
     print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}, "
           f"variants {len(variants)}, modes {len(modes)}, edge {len(edge)}")
 
 
+def reference_root(argv):
+    for a in argv:
+        if not a.startswith("--"):
+            return a
+    if os.environ.get("TREESA_REFERENCE"):
+        return os.environ["TREESA_REFERENCE"]
+    with open(os.path.join(ROOT, "BASELINE.json")) as f:
+        return json.load(f)["reference_path"]
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = reference_root(sys.argv[1:])
+    if "--baseline" in sys.argv:
+        path = os.path.join(HERE, "expected.json")
+        with open(path) as f:
+            exp = json.load(f)
+        exp["baseline"] = baseline(ref)
+        with open(path, "w") as f:
+            json.dump(exp, f, indent=1)
+    else:
+        main(ref)

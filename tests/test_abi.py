@@ -33,7 +33,8 @@ def test_ctypes_structs_match_the_library():
     sizes = (C.c_int32 * 3)()
     assert _abi.lib().tsa_abi_sizes(sizes) == 0
     assert list(sizes) == [C.sizeof(_abi.Instance), C.sizeof(_abi.Options), C.sizeof(_abi.Result)]
-    assert _abi.Options.timeout_s.offset == 220 and _abi.Options.reserved.offset == 224
+    assert _abi.Options.timeout_s.offset == 220 and _abi.Options.wait_log2.offset == 224
+    assert _abi.Options.debug_flags.offset == 228 and _abi.Options.reserved.offset == 232
 
 
 def _create(ixs, iy=(), nlab=None, **kw):
@@ -71,6 +72,10 @@ def test_argument_errors_are_reported_not_fatal():
     assert _create(tri, kernel_hint=3, par_follow=True)[0] == 1
     rc, msg = _create(tri, timeout_s=-1.0)
     assert rc == 1 and "timeout_s" in msg
+    rc, msg = _create(tri, wait_log2=5)
+    assert rc == 1 and "wait_log2" in msg
+    rc, msg = _create(tri, debug_flags=6)
+    assert rc == 1 and "debug_flags" in msg
     big = [[i, (i + 1) % 32769] for i in range(32769)]  # node ids are 16-bit: at most 32768 tensors
     rc, msg = _create(big)
     assert rc == 1 and "16-bit" in msg

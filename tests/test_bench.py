@@ -22,3 +22,56 @@ def test_reference_gpu_arm_without_the_binary_prints_unavailable(monkeypatch):
         rc = bench.reference_gpu_arm(bench.workload(8, "c2"), types.SimpleNamespace(steps=1, warmup=0), 0)
     line = json.loads(out.getvalue().strip().splitlines()[-1])
     assert rc == 0 and line["impl"] == "reference_gpu" and "unavailable" in line
+
+
+def test_instances_are_the_reference_generators_output(golden):
+    """sat(60, 1) / sat(100, 1) are the reference's tests/data/sat60.txt / sat100.txt (C1 / C2)."""
+    import workloads as WL
+    for n in (60, 100):
+        ixs, iy = WL.sat(n, 1)
+        assert ixs == golden[0][f"sat{n}"]["ixs"] and iy == []
+    ixs, iy, nlab = WL.instance("c5")
+    assert len(ixs) == 2454 and nlab == 576 and all(len(set(ix)) == 3 for ix in ixs)
+    ixs, iy, nlab = WL.instance("c3")
+    assert len(ixs) == 5000 and nlab == 2000
+
+
+def test_bench_start_trees_are_the_pinned_ones(golden):
+    """The start trees bench.py builds on the host (spectral search, greedy tree) are the ones whose
+    trajectories tests/golden pins against cpu_ref.h."""
+    import numpy as np
+
+    import workloads as WL
+    for e in golden[1]["baseline"]:
+        if "start_trees" not in e:
+            continue
+        W = WL.workload(e["nchains"], e["config"])
+        got = WL.start_trees(W["rec"], e["config"])
+        assert np.array_equal(got, np.array(e["start_trees"], np.uint32)), e["config"]
+
+
+def test_oracle_reproduces_the_full_size_cpu_ref_digests(golden):
+    """Our CPU restatement on C3 / C4 / C5 at full size (three levels of each schedule) against the
+    digests of the reference's cpu_ref.h."""
+    import numpy as np
+
+    import oracle as O
+    import workloads as WL
+    from tests import _util
+    for e in golden[1]["baseline"]:
+        if e["config"] not in ("c3", "c4", "c5"):
+            continue
+        ixs, iy, nlab = WL.instance(e["config"])
+        net = O.Net(ixs, iy, nlab)
+        st = np.array(e["start_trees"], np.uint32)
+        trees = np.stack([st[c % len(st)] for c in range(e["nchains"])])
+        S = None
+        if e.get("slices"):
+            S1 = np.zeros(net.nw, np.uint64)
+            for q in e["slices"]:
+                S1[q >> 6] |= np.uint64(1) << np.uint64(q & 63)
+            S = np.tile(S1, (e["nchains"], 1))
+        t, lab, cnt = O.sweeps(net, trees, np.asarray(e["betas"], np.float32), e["niters"], order=e["order"],
+                               seed=e["seed"], sc_target=e["sc_target"], S=S)
+        assert _util.digest(t, lab) == e["sha256"], e["config"]
+        assert cnt[0] == e["proposals"] and cnt[1] == e["accepts"]

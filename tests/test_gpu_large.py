@@ -1,19 +1,20 @@
 """Full-size checks of the CTA-per-chain kernel on the reference's large-lattice benchmark
 (bench/results/large_compare_gpu_par.jsonl): L x L lattice, row-major path start, par order, 72 chains x 20
 sweeps, betas 5:0.05:15, seed 1, pure tc (sc_target 10000).  The reference's GPU binary logged
-tc 44.209 / sc 33 (L=32) and 61.685 / 49 (L=48), identical on RTX 6000 and H100; with the device expf
+tc 44.209 / sc 33 (L=32), 61.685 / 49 (L=48) and 78.643 / 65 (L=64), identical on RTX 6000 and H100; with the device expf
 (the binary's Metropolis) this build reproduces them.  Also size-independent properties at the BASELINE
 sizes: the final labels equal the labels recomputed from the final topology for every chain."""
 import numpy as np
 import pytest
 
-from tests import _instances, _util
+import workloads as _instances
+from tests import _util
 from treesa_gpu_b200 import engine
 
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("L", [32, 48])
+@pytest.mark.parametrize("L", [32, 48, 64])
 def test_lattice_row_major_logged_result(L, golden):
     exp = [e for e in golden[1]["large"] if e["instance"] == f"sq{L}"][0]
     ixs, iy = _instances.sq(L)
@@ -36,7 +37,7 @@ def test_baseline_configs_keep_labels_consistent(cfg):
         ixs, iy = _instances.sq(64)
         kw = dict(nchains=16, scheme="indep")
     else:
-        ixs, iy = _instances.grid_ksat(24, 4.26, 1)
+        ixs, iy = _instances.grid_ksat(24, 4.26, 3, 1, seed=1)
         kw = dict(nchains=64, scheme="trunc", slicing=True, sc_target=30.0)
     net = engine.Network(ixs, iy)
     onet = O.Net(ixs, iy)

@@ -3,7 +3,8 @@ the host implementation in treesa_gpu_b200/spectral.py (the reference's spectral
 import numpy as np
 import pytest
 
-from tests import _instances, _util
+import workloads as _instances
+from tests import _util
 from treesa_gpu_b200 import engine, spectral
 
 pytestmark = pytest.mark.gpu

@@ -45,7 +45,7 @@ class Options(C.Structure):
                 ("exp_mode", C.c_int32), ("kernel_hint", C.c_int32), ("par_follow", C.c_int32),
                 ("par_band", C.c_int32), ("mode2", C.c_int32), ("niters2", C.c_int32),
                 ("betas2", C.POINTER(C.c_float)), ("nbetas2", C.c_int32), ("timeout_s", C.c_float),
-                ("reserved", C.c_int32 * 6)]
+                ("wait_log2", C.c_int32), ("debug_flags", C.c_int32), ("reserved", C.c_int32 * 4)]
 
 
 class Result(C.Structure):
@@ -106,7 +106,7 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
                  init_slices=(), select_sc=False, init_trees=None, gpu_model=None, h100_model=None, device=0,
                  stream=None, rank=0, world_size=1, nccl_id=None, verbose=False, max_levels=0, mode="tc",
                  exp_mode="host", kernel_hint=0, par_follow=False, par_band=0, betas2=None, niters2=0, mode2="gpu",
-                 timeout_s=0.0):
+                 timeout_s=0.0, wait_log2=0, debug_flags=0):
     o = Options()
     o.betas, _ = keep.arr(np.asarray(betas, np.float32), np.float32, C.c_float)
     o.nbetas = len(betas)
@@ -157,6 +157,8 @@ def make_options(keep, betas, niters, nchains, sc_target=20.0, sc_weight=1.0, sc
         o.niters2 = int(niters2 or 0)
         o.mode2 = MODE[mode2]
     o.timeout_s = float(timeout_s or 0.0)
+    o.wait_log2 = int(wait_log2)
+    o.debug_flags = int(debug_flags)
     return o
 
 

@@ -501,6 +501,8 @@ struct tsa_session {
   int cur_mode = 0;  // energy of the current level (score() depends on it)
   int slice_every = 1, max_slices = 0, select_sc = 0, verbose = 0, device = 0, rank = 0, world = 1, exp_device = 0;
   double timeout_s = 0;  // > 0: wall-clock limit of a run's level loop (single-GPU runs)
+  long long wait_cycles = 1ll << 31;  // limit of the kernels' bounded waits
+  int debug_arm_only = 0;             // tests: warp kernels arm the staging barrier without a copy
   double sc_target = 20, sc_weight = 1, trunc_frac = 0.25;
   uint64_t seed = 1;
   uint32_t key0 = 0, key1 = 0;
@@ -811,6 +813,18 @@ int tsa_session_create(const tsa_instance* inst, const tsa_options* O, tsa_sessi
     return TSA_ERR_ARG;
   }
   s->timeout_s = O->timeout_s;
+  if (O->wait_log2 != 0 && (O->wait_log2 < 10 || O->wait_log2 > 31)) {
+    set_err(err, errlen, "wait_log2 must be 0 (default, 2^31 cycles) or 10..31");
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  s->wait_cycles = 1ll << (O->wait_log2 ? O->wait_log2 : 31);
+  if (O->debug_flags & ~TSA_DEBUG_ARM_ONLY) {
+    set_err(err, errlen, "unknown debug_flags bits 0x%x", (unsigned)(O->debug_flags & ~TSA_DEBUG_ARM_ONLY));
+    delete s;
+    return TSA_ERR_ARG;
+  }
+  s->debug_arm_only = (O->debug_flags & TSA_DEBUG_ARM_ONLY) ? 1 : 0;
   bool model = false;
   for (int md : s->lmode) model = model || md != TSA_MODE_TC;
   if (O->kernel_hint == 3 && (s->par_band || s->par_follow || model)) {
@@ -951,6 +965,8 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.max_slices = s->max_slices;
   a.stats = s->d_stats;
   a.err = s->d_err;
+  a.wait_cycles = s->wait_cycles;
+  a.debug_arm_only = s->debug_arm_only;
   a.lse_tab = s->d_lse;
   a.leaf_sum = s->d_leaf_sum;
   a.scratch = s->d_scratch;

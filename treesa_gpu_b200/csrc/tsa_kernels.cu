@@ -65,8 +65,8 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Wait for phase `parity` of the mbarrier, for at most ~2^31 cycles (about a second).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for phase `parity` of the mbarrier, for at most `limit` SM cycles (2^31 by default: about a second).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long limit) {
   const long long t0 = clock64();
   for (;;) {
     uint32_t done;
@@ -76,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     if (done) return true;
-    if (clock64() - t0 > (1ll << 31)) return false;
+    if (clock64() - t0 > limit) return false;
   }
 }
 
@@ -710,9 +710,9 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
     if (lane == 0) {
       fence_proxy_async();
       mbar_expect_tx(&s_bar[warp], L.rec_bytes);
-      bulk_g2s(slot, grec, L.rec_bytes, &s_bar[warp]);
+      if (!a.debug_arm_only) bulk_g2s(slot, grec, L.rec_bytes, &s_bar[warp]);
     }
-    bool ok = mbar_wait(&s_bar[warp], phase);
+    bool ok = mbar_wait(&s_bar[warp], phase, a.wait_cycles);
     phase ^= 1u;
     if (!__all_sync(FULL, ok)) {
       if (lane == 0) atomicExch(a.err, 1);
@@ -1021,12 +1021,12 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
     if (pl == 0) {
       fence_proxy_async();
       mbar_expect_tx(&s_bar[pair], L.rec_bytes);
-      bulk_g2s(slot, grec, L.rec_bytes, &s_bar[pair]);
+      if (!a.debug_arm_only) bulk_g2s(slot, grec, L.rec_bytes, &s_bar[pair]);
     }
-    bool ok = mbar_wait(&s_bar[pair], phase);
+    bool ok = mbar_wait(&s_bar[pair], phase, a.wait_cycles);
     phase ^= 1u;
-    if (lane == 0 && !__all_sync(FULL, ok)) atomicOr(&pc[7], 1);
-    else if (lane != 0) (void)__all_sync(FULL, ok);
+    const bool all_ok = __all_sync(FULL, ok);
+    if (lane == 0 && !all_ok) atomicOr(&pc[7], 1);
     psync();
     if (pc[7]) {
       if (pl == 0) atomicExch(a.err, 1);

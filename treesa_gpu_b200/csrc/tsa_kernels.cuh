@@ -53,6 +53,8 @@ struct SweepArgs {
   int* out_ns;
   unsigned long long* stats; // 10 device counters (see tsa_session_stats; [7] is host-side)
   int* err;                  // nonzero: a bounded wait timed out
+  long long wait_cycles;     // limit of a bounded wait (SM cycles)
+  int debug_arm_only;        // tests: arm the staging barrier without issuing the copy
   const float* lse_tab;      // 64 floats (device)
   const uint64_t* leaf_sum;  // [m] chunk summaries of the leaf sets (when L.sums)
   int par_band;              // par order: 0, or L = 2..16 (priorities by depth band)

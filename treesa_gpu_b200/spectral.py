@@ -1,214 +1,233 @@
-"""Spectral start trees: linear orderings of the tensors from Laplacian eigenvectors, as path trees.
+"""Spectral start trees: tensor orderings from a low-frequency spectral embedding, as left-deep path trees.
 
-The annealer's local rotations rarely change a tree's global structure, so large networks need a good start.
-An ordering along a low-frequency Laplacian eigenvector of the tensor graph (spectral seriation; Fiedler)
-keeps cuts small without knowing the geometry.  Same role and interface as the reference's
-treesa_gpu/spectral.py (tensor_graph, laplacian_vectors, path_cost, path_tree, spectral_orders):
+The annealer's local rotations rarely change a tree's global structure, so large networks need a start
+whose cuts are already small.  The reference draws such starts from Laplacian eigenvectors of the tensor
+graph (treesa_gpu/spectral.py, called from treesa_gpu/driver.py:123-128 as ``spectral_orders(ixs, iy,
+k=spectral_k)``); this module keeps that interface -- a list of ``(tc, sc, order)``, best first, whose
+orders become path trees through ``path_tree`` -- and finds the orderings with its own search:
 
-* tensor graph: one vertex per tensor; a label shared by k tensors adds 1/(k-1) to each of its k(k-1)/2
-  pairs (weighted clique expansion of the hyperedge);
-* eigenvectors 1..3 of the graph Laplacian: dense ``numpy.linalg.eigh`` up to ``dense_max`` tensors, else
-  ``scipy.sparse.linalg.eigsh`` in shift-invert mode around 0;
-* candidate orderings sort the tensors by a direction in the span of the eigenvectors (a sweep of angles in
-  the (v1, v2) plane, refined around the best ones, plus random unit directions in (v1, v2, v3)), each in
-  both directions; every candidate path tree is scored exactly by ``path_cost``; the ``k`` best distinct
-  orderings are returned so that different chains can start from different trees.
+* graph: the hypergraph of the network (tensors = vertices, labels = hyperedges) expanded into cliques
+  through the sparse incidence matrix H, A = H diag(w) H^T off the diagonal, with w = 2/k for a label on k
+  tensors (a hyperedge adds the weight of one spanning tree, k - 1, spread over its k(k-1)/2 pairs);
+* embedding: the ``nvec`` lowest non-constant Laplacian eigenvectors; each coordinate is scaled by
+  1/sqrt(lambda), so that directions near the Fiedler vector dominate random draws.  Dense solver
+  (``scipy.linalg.eigh`` restricted to the wanted indices) up to ``dense_max`` tensors, sparse shift-invert
+  ``eigsh`` above, cuSOLVER on a device;
+* search: a small evolution strategy over unit directions u of the embedding.  A direction orders the
+  tensors by their projection, in both senses; generation 0 holds the coordinate axes and random
+  directions, each later generation perturbs the best directions found so far with a shrinking step.
+  Every generation is scored as one batch: one kernel launch on a device (``tsa_path_costs``), one
+  vectorised numpy pass otherwise (``path_costs``).
 
-The orderings depend on the eigensolver, so they are compared on tc, not as exact permutations.
-
-With a ``device``, both numerical parts run on that GPU through libtreesa_b200.so: the eigenvectors by
-cuSOLVER on the dense Laplacian (tsa_laplacian_vectors) and every batch of candidate orderings scored by
-one kernel launch (tsa_path_costs); the search itself is the same.
+Orderings depend on the eigensolver's rounding, so results are compared on tc, not as permutations.
 """
+import functools
 import math
 
 import numpy as np
 
 
-def tensor_graph(ixs):
-    """Weighted clique expansion as (n, rows, cols, w), every unordered pair once (rows < cols)."""
-    n = len(ixs)
-    occ = {}
+# ------------------------------------------------------------------------------------------------
+# graph and embedding
+# ------------------------------------------------------------------------------------------------
+def _incidence(ixs):
+    """(tensor ids, label ids) of every distinct (tensor, label) pair, and the labels (sorted) whose ids
+    those are."""
+    ts, ls = [], []
     for t, ix in enumerate(ixs):
-        for l in set(ix):
-            occ.setdefault(l, []).append(t)
-    acc = {}
-    for ts in occ.values():
-        k = len(ts)
-        if k < 2:
-            continue
-        w = 1.0 / (k - 1)
-        for a in range(k):
-            for b in range(a + 1, k):
-                key = (ts[a], ts[b]) if ts[a] < ts[b] else (ts[b], ts[a])
-                acc[key] = acc.get(key, 0.0) + w
-    if not acc:
+        for l in sorted(set(ix)):
+            ts.append(t)
+            ls.append(l)
+    ls = np.asarray(ls, np.int64)
+    uniq, lid = np.unique(ls, return_inverse=True) if len(ls) else (np.zeros(0, np.int64), ls)
+    return np.asarray(ts, np.int64), lid.astype(np.int64), uniq
+
+
+def tensor_graph(ixs):
+    """Weighted clique expansion of the network's hypergraph as (n, rows, cols, w), each pair once with
+    rows < cols; a label shared by k >= 2 tensors adds 2/k to each of its pairs."""
+    import scipy.sparse as sp
+    n = len(ixs)
+    ts, lid, labels = _incidence(ixs)
+    nl = len(labels)
+    if nl == 0:
         return n, np.zeros(0, np.int64), np.zeros(0, np.int64), np.zeros(0)
-    keys = np.array(list(acc.keys()), np.int64)
-    return n, keys[:, 0], keys[:, 1], np.array(list(acc.values()), np.float64)
+    H = sp.csr_matrix((np.ones(len(ts)), (ts, lid)), shape=(n, nl))
+    k = np.asarray(H.sum(0)).ravel()
+    lw = np.where(k >= 2, 2.0 / np.maximum(k, 1.0), 0.0)
+    A = sp.triu(H @ sp.diags(lw) @ H.T, k=1).tocoo()
+    keep = A.data > 0
+    return n, A.row[keep].astype(np.int64), A.col[keep].astype(np.int64), A.data[keep].astype(np.float64)
 
 
 def laplacian_vectors(n, rows, cols, w, k=3, dense_max=3000, seed=0, device=None):
-    """Eigenvectors 1..k (the lowest skipped) of the graph Laplacian, as the columns of an (n, k) array."""
+    """The eigenvectors of eigenvalues 2..k+1 (ascending; the constant one skipped) of the graph
+    Laplacian as the columns of an (n, k) array."""
     k = max(1, min(k, n - 2))
     if device is not None:
         from . import engine
         return engine.laplacian_vectors(n, rows, cols, w, k=k, device=device)
-    deg = np.zeros(n)
-    np.add.at(deg, rows, w)
-    np.add.at(deg, cols, w)
-    if n <= dense_max:
-        L = np.zeros((n, n))
-        L[rows, cols] -= w
-        L[cols, rows] -= w
-        L[np.arange(n), np.arange(n)] += deg
-        _, V = np.linalg.eigh(L)
-        return V[:, 1:k + 1]
     import scipy.sparse as sp
+    A = sp.coo_matrix((w, (rows, cols)), shape=(n, n))
+    A = (A + A.T).tocsr()
+    Lap = sp.diags(np.asarray(A.sum(1)).ravel()) - A
+    if n <= dense_max:
+        import scipy.linalg as la
+        _, V = la.eigh(Lap.toarray(), subset_by_index=[1, k])
+        return V
     import scipy.sparse.linalg as sla
-    L = sp.coo_matrix((np.concatenate([-w, -w, deg]),
-                       (np.concatenate([rows, cols, np.arange(n)]), np.concatenate([cols, rows, np.arange(n)]))),
-                      shape=(n, n)).tocsc()
-    rng = np.random.default_rng(seed)
-    vals, V = sla.eigsh(L, k=k + 1, sigma=-1e-3, which="LM", v0=rng.standard_normal(n))
-    o = np.argsort(vals)
-    return V[:, o[1:k + 1]]
+    v0 = np.random.default_rng(seed).standard_normal(n)
+    vals, V = sla.eigsh(Lap.tocsc(), k=k + 1, sigma=-1e-3, which="LM", v0=v0)
+    return V[:, np.argsort(vals)[1:k + 1]]
+
+
+def _rayleigh(V, rows, cols, w):
+    """lambda_j = v_j^T L v_j = sum over edges of w (v_j[r] - v_j[c])^2, for each column."""
+    d = V[rows] - V[cols]
+    return (w[:, None] * d * d).sum(0)
+
+
+# ------------------------------------------------------------------------------------------------
+# path trees and their cost
+# ------------------------------------------------------------------------------------------------
+def path_tree(order):
+    """Left-deep tree dict contracting the tensors in ``order`` left to right."""
+    leaves = [{"tensor_index": int(t)} for t in order]
+    return functools.reduce(lambda acc, leaf: {"args": [acc, leaf]}, leaves[1:], leaves[0])
+
+
+class _PathScorer:
+    """Vectorised exact (tc, sc) of the path trees of a batch of orderings on the host.
+
+    Contraction step i (1 <= i < m) joins the prefix order[0..i-1] with tensor order[i].  With f and e a
+    label's first position and its end (last position, or m when the label is open), the prefix carries
+    the labels with f <= i-1 < e (at step 1 the prefix is the leaf order[0], which carries every label
+    with f == 0), the tensor brings the labels with f == i in addition, and the step's output keeps the
+    labels with f <= i < e.  tc = log2 sum_i 2^|step i|; sc = max(outputs, every input tensor)."""
+
+    def __init__(self, ixs, iy=()):
+        self.m = len(ixs)
+        self.ts, self.lid, labels = _incidence(ixs)
+        self.nl = len(labels)
+        order = np.lexsort((self.ts, self.lid))
+        self.occ_t = self.ts[order]
+        lsorted = self.lid[order]
+        self.starts = np.flatnonzero(np.r_[True, lsorted[1:] != lsorted[:-1]]) if len(lsorted) else np.zeros(0, int)
+        opened = set(int(l) for l in iy)
+        self.open = np.array([int(l) in opened for l in labels], bool)
+        self.max_in = max((len(set(ix)) for ix in ixs), default=0)
+
+    def __call__(self, orders):
+        orders = np.atleast_2d(np.asarray(orders, np.int64))
+        B, m = orders.shape
+        if m < 2:
+            return [(0.0, self.max_in)] * B
+        if self.nl == 0:
+            return [(math.log2(m - 1), self.max_in)] * B
+        pos = np.empty_like(orders)
+        pos[np.arange(B)[:, None], orders] = np.arange(m)[None, :]
+        P = pos[:, self.occ_t]
+        f = np.minimum.reduceat(P, self.starts, axis=1)
+        e = np.where(self.open[None, :], m, np.maximum.reduceat(P, self.starts, axis=1))
+        # live[b, c] = #{labels: f <= c < e}, by +1 at f and -1 at e, summed along the positions
+        row = (np.arange(B) * (m + 1))[:, None]
+        delta = np.zeros(B * (m + 1), np.int64)
+        np.add.at(delta, (row + f).ravel(), 1)
+        np.add.at(delta, (row + e).ravel(), -1)
+        live = np.cumsum(delta.reshape(B, m + 1), axis=1)[:, :m]
+        born = np.zeros(B * m, np.int64)
+        np.add.at(born, (np.arange(B)[:, None] * m + f).ravel(), 1)
+        born = born.reshape(B, m)
+        left = live[:, :m - 1].copy()
+        left[:, 0] = born[:, 0]
+        step = left + born[:, 1:]
+        hi = step.max(1)
+        tc = hi + np.log2(np.exp2(step - hi[:, None]).sum(1))
+        sc = np.maximum(live[:, 1:].max(1), self.max_in)
+        return [(float(a), int(b)) for a, b in zip(tc, sc)]
+
+
+def path_costs(orders, ixs, iy=()):
+    """[(tc, sc)] in log2 of the path trees of a batch of orderings (host, vectorised)."""
+    return _PathScorer(ixs, iy)(orders)
 
 
 def path_cost(order, ixs, iy=()):
-    """(tc, sc) in log2 of the path tree contracting the tensors in ``order`` left to right.
-
-    Step i >= 1 contracts the prefix order[0..i-1] with tensor order[i]; its cost is the number of distinct
-    labels involved: the labels alive across the cut (first occurrence before i, last at or after i) plus
-    those first seen at i (step 1: the union of the first two tensors).  Output of step i: the labels
-    alive across the cut after position i (open labels stay alive to the end)."""
-    m = len(order)
-    if m < 2:
-        return 0.0, max((len(set(ix)) for ix in ixs), default=0)
-    pos = np.empty(m, np.int64)
-    pos[np.asarray(order, np.int64)] = np.arange(m)
-    first, last = {}, {}
-    for t, ix in enumerate(ixs):
-        p = int(pos[t])
-        for l in ix:
-            if l not in first or p < first[l]:
-                first[l] = p
-            if l not in last or p > last[l]:
-                last[l] = p
-    opened = set(iy)
-    labs = list(first)
-    f = np.array([first[l] for l in labs], np.int64)
-    la = np.array([m if l in opened else last[l] for l in labs], np.int64)
-    # alive[c]: labels with first < c <= last  (crossing the cut between positions c-1 and c)
-    diff = np.zeros(m + 2, np.int64)
-    np.add.at(diff, f + 1, 1)
-    np.add.at(diff, la + 1, -1)
-    alive = np.cumsum(diff)[:m + 1]
-    newc = np.bincount(f, minlength=m)
-    cost = alive[1:m] + newc[1:m]
-    cost[0] = len(set(ixs[order[0]]) | set(ixs[order[1]]))
-    outs = alive[2:m + 1]
-    sc = int(max(int(outs.max()), max(len(set(ix)) for ix in ixs)))
-    cm = int(cost.max())
-    tc = cm + math.log2(float(np.sum(np.exp2(cost - cm))))
-    return tc, sc
+    """(tc, sc) in log2 of the path tree contracting the tensors in ``order`` left to right."""
+    return _PathScorer(ixs, iy)([list(order)])[0]
 
 
-def path_tree(order):
-    """Left-deep tree dict contracting the tensors in ``order``."""
-    t = {"tensor_index": int(order[0])}
-    for i in order[1:]:
-        t = {"args": [t, {"tensor_index": int(i)}]}
-    return t
-
-
-def _gpu_scorer(ixs, iy, device):
-    """score(list of orderings) -> list of (tc, sc), one kernel launch per call."""
+def _device_scorer(ixs, iy, device):
+    """score(batch of orderings) -> [(tc, sc)] by one tsa_path_costs launch."""
     from . import engine
-    lmap = {}
-    for ix in ixs:
-        for l in ix:
-            lmap.setdefault(l, len(lmap))
-    for l in iy:
-        lmap.setdefault(l, len(lmap))
-    net = engine.Network([[lmap[l] for l in ix] for ix in ixs], [lmap[l] for l in iy], max(1, len(lmap)))
+    ids = {}
+    for l in [l for ix in ixs for l in ix] + list(iy):
+        ids.setdefault(l, len(ids))
+    net = engine.Network([[ids[l] for l in ix] for ix in ixs], [ids[l] for l in iy], max(1, len(ids)))
 
     def score(orders):
-        tc, sc = engine.path_costs(net, np.array(orders, np.int32), device=device)
+        tc, sc = engine.path_costs(net, np.asarray(orders, np.int32), device=device)
         return [(float(a), int(b)) for a, b in zip(tc, sc)]
     return score
 
 
-def spectral_orders(ixs, iy=(), k=8, nangles=24, nrandom=24, seed=0, dense_max=3000, device=None):
-    """The ``k`` best distinct spectral orderings: list of (tc, sc, order), best first.  With a ``device``
-    the eigenvectors and the path costs are computed on that GPU."""
+# ------------------------------------------------------------------------------------------------
+# the search
+# ------------------------------------------------------------------------------------------------
+def spectral_orders(ixs, iy=(), k=4, nvec=6, batch=64, generations=16, nelite=6, step=0.35, seed=0,
+                    dense_max=3000, device=None):
+    """The ``k`` best distinct orderings found, as a list of (tc, sc, order), best first.
+
+    nvec        eigenvectors spanning the embedding
+    batch       directions per generation (each scored in both senses)
+    generations rounds of the evolution strategy after generation 0
+    nelite      directions kept as parents of the next generation
+    step        initial perturbation size (relative to a unit direction), halved every two generations
+    With a ``device`` the eigenvectors and every generation's path costs are computed on that GPU."""
     n = len(ixs)
     if n < 3:
-        return [(0.0, 0, list(range(n)))]
+        return [(0.0, max((len(set(ix)) for ix in ixs), default=0), list(range(n)))]
     n_, rows, cols, w = tensor_graph(ixs)
-    V = laplacian_vectors(n, rows, cols, w, k=3, dense_max=dense_max, seed=seed, device=device)
+    V = laplacian_vectors(n, rows, cols, w, k=nvec, dense_max=dense_max, seed=seed, device=device)
     d = V.shape[1]
+    lam = _rayleigh(V, rows, cols, w) if len(w) else np.ones(d)
+    E = V / np.sqrt(np.maximum(lam, 1e-12 * max(1.0, float(lam.max()))))[None, :]
+    score = _device_scorer(ixs, iy, device) if device is not None else _PathScorer(ixs, iy)
     rng = np.random.default_rng(seed)
-    cands, seen = [], set()
-    if device is not None:
-        score = _gpu_scorer(ixs, iy, device)
-    else:
-        def score(orders):
-            return [path_cost(o, ixs, iy) for o in orders]
+    found = {}  # ordering bytes -> (tc, sc, serial, order, direction)
 
-    def try_dirs(vs):
-        """Candidates of the directions vs (both senses each), scored together; best tc per direction."""
-        todo, owner = [], []
-        for j, v in enumerate(vs):
-            o = np.argsort(V @ v, kind="stable")
+    def evaluate(dirs):
+        todo, src = [], []
+        for u in dirs:
+            o = np.argsort(E @ u, kind="stable")
             for oo in (o, o[::-1]):
                 key = oo.tobytes()
-                if key in seen:
-                    continue
-                seen.add(key)
-                todo.append(oo.tolist())
-                owner.append(j)
-        best = [None] * len(vs)
-        for (tc, sc), oo, j in zip(score(todo) if todo else [], todo, owner):
-            cands.append((tc, sc, oo, np.array(vs[j], float)))
-            best[j] = tc if best[j] is None else min(best[j], tc)
-        return best
+                if key not in found:
+                    found[key] = None
+                    todo.append(oo)
+                    src.append(u)
+        if not todo:
+            return
+        for (tc, sc), oo, u in zip(score(np.stack(todo)), todo, src):
+            found[oo.tobytes()] = (tc, sc, len(found), oo, u)
 
-    def try_dir(v):
-        return try_dirs([v])[0]
+    def ranked():
+        return sorted((v for v in found.values() if v is not None), key=lambda c: (c[0], c[1], c[2]))
 
-    def plane(th):
-        v = np.zeros(d)
-        v[0], v[1] = math.cos(th), math.sin(th)
-        return v
-
-    first = [plane(math.pi * a / nangles) for a in range(nangles)] if d >= 2 else [np.ones(1)]
-    for _ in range(nrandom if d >= 3 else 0):
-        v = rng.standard_normal(d)
-        first.append(v / np.linalg.norm(v))
-    try_dirs(first)
-    if d >= 2:
-        # local refinement of the angle around the three best plane directions (a small tilt orders the
-        # sites inside a wavefront on lattices)
-        plane_c = sorted([c for c in cands if np.count_nonzero(c[3][2:]) == 0], key=lambda c: (c[0], c[1]))
-        starts = []
-        for c in plane_c:
-            th = math.atan2(c[3][1], c[3][0])
-            if all(abs(th - t0) > 1e-9 for t0 in starts):
-                starts.append(th)
-            if len(starts) == 3:
+    unit = lambda x: x / max(np.linalg.norm(x), 1e-300)  # noqa: E731
+    gen0 = [np.eye(d)[j] for j in range(d)]
+    gen0 += [unit(rng.standard_normal(d)) for _ in range(max(0, batch - d))]
+    evaluate(gen0)
+    sigma = step
+    for g in range(generations):
+        parents = []
+        for c in ranked():
+            if not any(np.allclose(c[4], p) for p in parents):
+                parents.append(c[4])
+            if len(parents) == nelite:
                 break
-        for th0 in starts:
-            th, step = th0, math.pi / nangles / 2
-            cur = min(c[0] for c in plane_c if abs(math.atan2(c[3][1], c[3][0]) - th0) < 1e-9)
-            for _ in range(8):
-                moved = False
-                for dth in (-step, step):
-                    t = try_dir(plane(th + dth))
-                    if t is not None and t < cur - 1e-9:
-                        cur, th, moved = t, th + dth, True
-                        break
-                if not moved:
-                    step /= 2
-    cands.sort(key=lambda c: (c[0], c[1]))
-    return [(c[0], c[1], c[2]) for c in cands[:k]]
+        kids = [unit(parents[i % len(parents)] + sigma * rng.standard_normal(d)) for i in range(batch)]
+        evaluate(kids)
+        if g % 2 == 1:
+            sigma *= 0.5
+    return [(c[0], c[1], c[3].tolist()) for c in ranked()[:k]]
