@@ -132,3 +132,32 @@ def test_time_models_match_reference_formulas():
     cc = M["cc_bit"] * (a + b + c) + M["cc_cell"] * 2.0 ** 26
     tcv = M["tc_bit"] * (a + b + c) + M["tc_pad_cell"] * 2.0 ** (5 + 6 + 7 + 8) + M["tc_out_bit"] * c
     assert abs(h - (3 * M["launch"] + 2 * (a + b) / M["perm_bw_bits"] + min(cc, tcv))) < 1e-18
+
+
+def _subtrees(ch, m):
+    under, out = {}, set()
+    for i, (l, r) in enumerate(ch):
+        s = (frozenset([l]) if l < m else under[l]) | (frozenset([r]) if r < m else under[r])
+        under[m + i] = s
+        out.add(s)
+    return out
+
+
+@pytest.mark.parametrize("name", ["sat40", "sat60", "sat100", "reg3_100", "reg3_250", "lat10", "lat14", "grid24",
+                                  "grid28"])
+def test_greedy_tree_equals_omeco_greedy_fixture(name):
+    """The reference's tests/data/<inst>.tree files hold omeco's GreedyMethod trees (driver.py:117-122,
+    the reference's greedy start); the restatement in driver._greedy_children builds the same tree: the
+    same set of contracted tensor groups (child order aside)."""
+    rec = _util.instance(name)
+    m = rec["m"]
+    ch = driver._greedy_children([list(ix) for ix in rec["ixs"]], list(rec["iy"]))
+    assert _subtrees(ch, m) == _subtrees([tuple(x) for x in rec["tree"]], m)
+
+
+def test_sq46_fixture_is_the_row_major_path():
+    """sq46.tree is not a greedy tree: the reference's checks start sq46 from the row-major path
+    (tests/run_checks.sh names those runs "sweep")."""
+    import workloads as WL
+    rec = _util.instance("sq46")
+    assert (_util.words(rec["tree"]) == WL.path_words(list(range(rec["m"])), rec["m"])).all()

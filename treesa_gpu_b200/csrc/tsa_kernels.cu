@@ -198,6 +198,27 @@ struct ChainCounters {
     *this = ChainCounters{};
   }
 };
+// per-chain counts of one thread of the CTA kernels (32 bits: a thread's share of one chain), added into
+// the launch's device counters at the end of every chain, so that no 64-bit totals stay live in registers
+struct BlkCounters {
+  uint32_t prop, acc, steps, visits, sprop, sacc, busy, chunks, chunks_acc;
+  // every thread: its own proposals/accepts/visits/items; steps counted by one thread; slice moves by all
+  // 32 lanes of warp 0 (slice_div 32), or by two CTAs of which one reports (slice_div 0 in the other)
+  __device__ __forceinline__ void flush(unsigned long long* stats, int slice_div) {
+    uint32_t v[9] = {prop, acc, steps, visits, sprop, sacc, busy, chunks, chunks_acc};
+#pragma unroll
+    for (int q = 0; q < 9; q++) v[q] = __reduce_add_sync(0xFFFFFFFFu, v[q]);
+    if ((threadIdx.x & 31) == 0) {
+      v[4] = slice_div ? v[4] / (uint32_t)slice_div : 0u;
+      v[5] = slice_div ? v[5] / (uint32_t)slice_div : 0u;
+      const int slot[9] = {0, 1, 2, 3, 4, 5, 6, 8, 9};
+#pragma unroll
+      for (int q = 0; q < 9; q++)
+        if (v[q]) atomicAdd(&stats[slot[q]], (unsigned long long)v[q]);
+    }
+    *this = BlkCounters{};
+  }
+};
 
 // Metropolis: host-libm-exact (default) or with the device's expf as the reference's GPU binary
 __device__ __forceinline__ bool accept_rt(int exp_device, float beta, const double* exptab, uint32_t r, float dE) {
@@ -1341,7 +1362,7 @@ __device__ __forceinline__ void follow_rearm(const FollowCtx* f, int Pn, int m) 
 // sweep: the Philox sweep counter of this visit; fol: re-arm on accept (a first visit with par_follow)
 template <bool SUMS, bool PAR, bool MODEL = false>
 __device__ __forceinline__ void visit_coop(const BlkCtx& B, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
-                                           int G, int t, unsigned gm, Counters& cnt,
+                                           int G, int t, unsigned gm, BlkCounters& cnt,
                                            const FollowCtx* fol = nullptr) {
   const int m = B.m, i = v - m, nw = B.nw;
   uint32_t chv = B.ch[i];
@@ -1534,7 +1555,7 @@ __device__ __forceinline__ int nth_label_rt(const uint64_t* A, const uint64_t* S
 // proposed slice set.
 // costs: scratch for the model modes' node costs (null in tc mode)
 __device__ void slice_step_block(const BlkCtx& B, const SweepArgs& a, uint32_t* cz2, int* sh, float* shf,
-                                 uint32_t sweep, uint32_t chain, Counters& cnt, float* costs = nullptr) {
+                                 uint32_t sweep, uint32_t chain, BlkCounters& cnt, float* costs = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, T = blockDim.x, m = B.m, nw = B.nw;
   EvalOut cur{};
   float Ecur = 0.f;
@@ -1709,12 +1730,12 @@ __device__ __forceinline__ int pick_group(int k, int T) {
 // dependent HBM/L2 round trip per chunk.  Here the phase's nodes are taken in batches of kFlatBatch:
 //   1. one owner thread per node draws the rule (Philox), finds P, O, K, M and the chunk union u;
 //   2. a block-wide exclusive scan of popc(u) numbers the batch's chunk items;
-//   3. every thread takes items e = tid, tid + T, ... (two at a time, all eight 16-byte loads issued
+//   3. every thread takes items e = tid, tid + T, ... (IPT at a time, all 4 IPT 16-byte loads issued
 //      before any is used), finds each item's node by a binary search over the batch's item offsets
 //      and its chunk as the k-th set bit of u, and adds the item's popcounts (sx | k2 << 16, k3) and
 //      nonzero bit of X into the node's shared-memory totals with 32-bit atomics;
 //   4. the owner evaluates dE and the Metropolis test and rewrites the node's metadata on accept;
-//   5. X is stored into P's chunks for the items of accepted nodes (a thread's first two items from
+//   5. X is stored into P's chunks for the items of accepted nodes (a thread's first IPT items from
 //      registers, any further ones recomputed: the sets they read are unchanged by the phase).
 // Same moves, same random numbers and the same integer counts as visit_coop, so the chains are
 // bit-identical; only the schedule of the loads changes.
@@ -1865,9 +1886,10 @@ __device__ __forceinline__ void flat_store(const BlkCtx& B, const FlatTabs& F, I
 }
 
 // CL = 2: one CTA of a pair; metadata writes go to both CTAs' copies (P: the other CTA's arrays).
-template <bool PAR, int CL>
+// IPT: items a thread has in flight at once (their loads are all issued before the first is used).
+template <bool PAR, int CL, int IPT = 2>
 __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl, uint16_t* pri, uint16_t* par,
-                               int nk, uint32_t sweep, uint32_t chain, Counters& cnt, const PeerArrays& P,
+                               int nk, uint32_t sweep, uint32_t chain, BlkCounters& cnt, const PeerArrays& P,
                                const FollowCtx* fol = nullptr) {
   const int tid = threadIdx.x, T = blockDim.x, lane = tid & 31, warp = tid >> 5, nwarps = T >> 5;
   const int m = B.m;
@@ -1923,11 +1945,16 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     }
     if (tid < nb) F.off[tid] = (uint32_t)(incl - nck + before);
     __syncthreads();
-    // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first two items.  A batch of
-    // at most 2T items decodes each item's node and chunk directly (no list)
-    Item k0{-1, 0}, k1{-1, 0};
-    ulonglong2 x0 = make_ulonglong2(0ull, 0ull), x1 = x0;
-    const bool direct = total <= 2 * T;
+    // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first IPT items.  A batch
+    // of at most IPT * T items decodes each item's node and chunk directly (no list)
+    Item kk[IPT];
+    ulonglong2 kx[IPT];
+#pragma unroll
+    for (int i = 0; i < IPT; i++) {
+      kk[i] = Item{-1, 0};
+      kx[i] = make_ulonglong2(0ull, 0ull);
+    }
+    const bool direct = total <= IPT * T;
     for (int w0 = 0; w0 < total; w0 += kFlatItems) {
       if (!direct) {
         if (w0) __syncthreads();  // the previous window's items are consumed
@@ -1936,31 +1963,25 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       }
       const int nwin = min(kFlatItems, total - w0);
       auto item = [&](int e) { return direct ? flat_decode(F, nb, e) : item_of(F.items[e]); };
-      int e = tid;
-      for (; e + T < nwin; e += 2 * T) {  // two items: all eight loads issued before either is used
-        const Item i0 = item(e), i1 = item(e + T);
-        const ItemSets s0 = flat_load<CL>(B, F, wlb, i0);
-        const ItemSets s1 = flat_load<CL>(B, F, wlb, i1);
-        const ItemX r0 = flat_compute(B, i0, s0), r1 = flat_compute(B, i1, s1);
-        flat_add(F, i0.j, r0);
-        flat_add(F, i1.j, r1);
-        if (w0 == 0 && e == tid) {
-          k0 = i0;
-          x0 = r0.x;
-          k1 = i1;
-          x1 = r1.x;
+      for (int e = tid; e < nwin; e += IPT * T) {  // IPT items: all their loads issued before any is used
+        Item it[IPT];
+        ItemSets sv[IPT];
+#pragma unroll
+        for (int i = 0; i < IPT; i++) it[i] = e + i * T < nwin ? item(e + i * T) : Item{-1, 0};
+#pragma unroll
+        for (int i = 0; i < IPT; i++)
+          if (it[i].j >= 0) sv[i] = flat_load<CL>(B, F, wlb, it[i]);
+#pragma unroll
+        for (int i = 0; i < IPT; i++) {
+          if (it[i].j < 0) continue;
+          const ItemX r = flat_compute(B, it[i], sv[i]);
+          flat_add(F, it[i].j, r);
+          if (w0 == 0 && e == tid) {
+            kk[i] = it[i];
+            kx[i] = r.x;
+          }
+          cnt.busy++;
         }
-        cnt.busy += 2;
-      }
-      if (e < nwin) {
-        const Item i0 = item(e);
-        const ItemX r0 = flat_eval<CL>(B, F, wlb, i0);
-        flat_add(F, i0.j, r0);
-        if (w0 == 0 && e == tid) {
-          k0 = i0;
-          x0 = r0.x;
-        }
-        cnt.busy++;
       }
     }
     __syncthreads();
@@ -2007,12 +2028,13 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       cnt.visits++;
     }
     __syncthreads();
-    // 5. X into the pivots of accepted moves: the two kept items from registers, the rest recomputed
-    if (k0.j >= 0 && F.acc[k0.j]) flat_store(B, F, k0, x0);
-    if (k1.j >= 0 && F.acc[k1.j]) flat_store(B, F, k1, x1);
+    // 5. X into the pivots of accepted moves: the kept items from registers, the rest recomputed
+#pragma unroll
+    for (int i = 0; i < IPT; i++)
+      if (kk[i].j >= 0 && F.acc[kk[i].j]) flat_store(B, F, kk[i], kx[i]);
     const bool rebuild = total > kFlatItems;  // the list in shared memory is the last window's
     for (int w0 = 0; w0 < total; w0 += kFlatItems) {
-      const int first = w0 == 0 ? 2 * T : 0;  // window 0's items [0, 2T) were kept in registers
+      const int first = w0 == 0 ? IPT * T : 0;  // window 0's items [0, IPT T) were kept in registers
       const int nwin = min(kFlatItems, total - w0);
       if (nwin <= first) continue;  // uniform
       if (rebuild) {
@@ -2027,8 +2049,8 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     }
     // The next batch rewrites the tables at once, so it waits for the stores.  After the last batch the
     // caller's next phase writes wl and the tables only behind its own scan barrier, and the stores of a
-    // batch of at most 2T items read neither (X and the items come from registers): no barrier then.
-    if (b0 + NB < nk || total > 2 * T) __syncthreads();
+    // batch of at most IPT T items read neither (X and the items come from registers): no barrier then.
+    if (b0 + NB < nk || total > IPT * T) __syncthreads();
   }
 }
 
@@ -2095,7 +2117,7 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
     for (int q = tid; q < L.m; q += T) ls[q] = a.leaf_sum[q];
     B.leaf_sum = ls;
   }
-  Counters cnt{};
+  BlkCounters cnt{};
   __syncthreads();
   for (int c = blockIdx.x; c < a.nchains; c += gridDim.x) {
     uint8_t* grec = a.recs + (size_t)c * L.rec_bytes;
@@ -2270,23 +2292,8 @@ __global__ void __launch_bounds__(512, 1) k_anneal_block(SweepArgs a) {
       }
     }
     for (int q = tid; q < L.nw; q += T) wS[q] = B.S[q];
+    cnt.flush(a.stats, 32);  // slice moves were counted by all 32 lanes of warp 0
     __syncthreads();
-  }
-  // every thread: its own proposals/accepts/visits; steps and slice moves counted by one thread/warp
-  unsigned long long v[9] = {cnt.prop,  cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc,
-                             cnt.busy, cnt.chunks, cnt.chunks_acc};
-#pragma unroll
-  for (int q = 0; q < 9; q++) {
-    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(FULL, v[q], o);
-  }
-  if (lane == 0) {
-    // slice moves were counted by all 32 lanes of warp 0
-    v[4] /= 32;
-    v[5] /= 32;
-    const int slot[9] = {0, 1, 2, 3, 4, 5, 6, 8, 9};
-#pragma unroll
-    for (int q = 0; q < 9; q++)
-      if (v[q]) atomicAdd(&a.stats[slot[q]], v[q]);
   }
 }
 
@@ -2361,14 +2368,18 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
     for (int q = tid; q < L.m; q += T) ls[q] = a.leaf_sum[q];
     B.leaf_sum = ls;
   }
-  PeerArrays P;
-  P.ch = cl.map_shared_rank(B.ch, rank ^ 1);
-  P.cz = cl.map_shared_rank(B.cz, rank ^ 1);
-  P.sum = cl.map_shared_rank(B.sum, rank ^ 1);
-  P.par = cl.map_shared_rank(par, rank ^ 1);
-  P.pri = cl.map_shared_rank(pri, rank ^ 1);
+  // the other CTA's array bases live in this CTA's block scalars (bytes 64..103 of that area), read when a
+  // decision writes both copies, so that they hold no registers through the rest of a phase
+  PeerArrays& P = *reinterpret_cast<PeerArrays*>(smem + 768 + 64);
+  if (tid == 0) {
+    P.ch = cl.map_shared_rank(B.ch, rank ^ 1);
+    P.cz = cl.map_shared_rank(B.cz, rank ^ 1);
+    P.sum = cl.map_shared_rank(B.sum, rank ^ 1);
+    P.par = cl.map_shared_rank(par, rank ^ 1);
+    P.pri = cl.map_shared_rank(pri, rank ^ 1);
+  }
   int* peer_sh = cl.map_shared_rank(sh, rank ^ 1);
-  Counters cnt{};
+  BlkCounters cnt{};
   const int npair = (int)(gridDim.x / 2);
   for (int c = (int)(blockIdx.x / 2); c < a.nchains; c += npair) {
     uint8_t* grec = a.recs + (size_t)c * L.rec_bytes;
@@ -2460,25 +2471,11 @@ __global__ void __launch_bounds__(512, 1) k_anneal_cluster(SweepArgs a) {
       }
       for (int q = tid; q < L.nw; q += T) wS[q] = B.S[q];
     }
+    cnt.flush(a.stats, rank == 0 ? 32 : 0);  // slice moves: all 32 lanes of warp 0 of both CTAs
     __syncthreads();
   }
   // the peer may still write into this CTA's shared memory until both have left the last phase
   cl.sync();
-  unsigned long long v[9] = {cnt.prop,  cnt.acc, cnt.steps, cnt.visits, cnt.sprop, cnt.sacc,
-                             cnt.busy, cnt.chunks, cnt.chunks_acc};
-#pragma unroll
-  for (int q = 0; q < 9; q++) {
-    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(FULL, v[q], o);
-  }
-  if (lane == 0) {
-    // slice moves were counted by all 32 lanes of warp 0 of both CTAs
-    v[4] = rank == 0 ? v[4] / 32 : 0;
-    v[5] = rank == 0 ? v[5] / 32 : 0;
-    const int slot[9] = {0, 1, 2, 3, 4, 5, 6, 8, 9};
-#pragma unroll
-    for (int q = 0; q < 9; q++)
-      if (v[q]) atomicAdd(&a.stats[slot[q]], v[q]);
-  }
 }
 
 // Population resampling: dst chain c <- src chain anc[c] (reference k_copy, :1017-1022).
