@@ -108,6 +108,70 @@ def reference_gpu_arm(W, args, device):
     return 0
 
 
+def tc_at_wall(W, budget, device, scale="chains"):
+    """BASELINE's second metric: the best tc (log2) each implementation reaches within `budget` seconds of
+    wall time on the config's workload.  The schedule and start trees stay the config's; each
+    implementation runs the largest population (scale "chains", in multiples of 32; best-of-N over more
+    chains is the way a fixed budget buys a better expected best) or the most sweeps per beta level (scale
+    "sweeps") that its calibrated wall time fits into the budget.  Ours is timed around one tsa_run call
+    (host init, upload, anneal, download, finalize); the reference's GPU binary around its CLI process
+    (input files written beforehand)."""
+    import tempfile
+
+    from treesa_gpu_b200 import engine
+    rec = W["rec"]
+    trees = start_trees(rec, config=W["config"])
+    net = engine.Network(rec["ixs"], rec["iy"], rec["nlab"])
+
+    key = "nchains" if scale == "chains" else "niters"
+    unit = 32 if scale == "chains" else 1
+    n0 = W[key]
+
+    def ours(n):
+        opts = dict(betas=W["betas"], niters=W["niters"], nchains=W["nchains"], sc_target=W["sc_target"],
+                    order=W["order"], scheme=W["scheme"], seed=W["seed"], init_trees=trees, device=device,
+                    slicing=W["slicing"])
+        opts[key] = n
+        t0 = time.time()
+        rc, d = engine.run(net, **opts)
+        return time.time() - t0, d["tc"], d["sc"]
+
+    def ref(n, workdir):
+        _, wall, res = reference_gpu_run(dict(W, **{key: n}), trees, workdir, device)
+        return wall, res.get("tc"), res.get("sc")
+
+    def fit(run):
+        """Wall time is affine in the scaled quantity: two calibration runs, then runs that home in on
+        [0.85, 1.0] x budget (at most five)."""
+        run(n0)  # warm-up (context, caches)
+        a, b = max(unit, n0 // 2 // unit * unit), 2 * n0
+        ta, tb = run(a)[0], run(b)[0]
+        slope = max((tb - ta) / (b - a), 1e-9)
+        fixed = max(0.0, ta - a * slope)
+        n = max(unit, int((budget - fixed) / slope) // unit * unit)
+        best = None
+        for _ in range(5):
+            w, tc, sc = run(n)
+            if w <= budget:
+                best = dict(n=n, wall_s=w, tc=tc, sc=sc)
+                if w >= 0.85 * budget:
+                    break
+                n = max(n + unit, int(n * (budget - fixed) / max(w - fixed, 1e-6) * 0.97) // unit * unit)
+            else:
+                n = max(unit, int(n * (budget - fixed) / max(w - fixed, 1e-6) * 0.95) // unit * unit)
+        return dict(best or dict(n=n, wall_s=w, tc=tc, sc=sc, over_budget=True), scaled=key)
+
+    out = {"metric": "best tc (log2) at fixed wall time", "unit": "log2 flops", "higher_is_better": False,
+           "config": config_dict(W, 1), "wall_budget_s": budget, "scale": scale, "ours": fit(ours)}
+    if os.path.exists(REF_GPU):
+        with tempfile.TemporaryDirectory() as d:
+            out["reference_gpu"] = fit(lambda n: ref(n, d))
+    else:
+        out["reference_gpu"] = {"unavailable": "oracle/_ref/treesa_gpu_ref not built"}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def visits_per_step(W, world):
     return len(W["betas"]) * W["niters"] * W["nchains"] * world * (W["rec"]["m"] - 1)
 
@@ -234,6 +298,11 @@ def main():
     ap.add_argument("--levels", default="", help="profiling runs only: the first L beta levels (L), or levels "
                                                    "a..b-1 of the schedule (a:b)")
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS), help="BASELINE config (default c2)")
+    ap.add_argument("--tc-scale", default="chains", choices=["chains", "sweeps"],
+                    help="--tc-at-wall: what the budget buys, more chains (default) or more sweeps per level")
+    ap.add_argument("--tc-at-wall", type=float, default=0.0,
+                    help="instead of the throughput line: best tc of ours and of the reference's GPU binary within "
+                         "this many seconds of wall time (BASELINE's second metric)")
     ap.add_argument("--order", default="", choices=["", "par", "preorder"],
                     help="sweep order instead of the config's (a side measurement, not a BASELINE config)")
     args = ap.parse_args()
@@ -275,6 +344,13 @@ def main():
             return 0
         return reference_gpu_arm(W, args, local)
 
+    if args.tc_at_wall > 0:
+        if rank != 0 or world > 1:
+            return 0
+        import torch
+        torch.cuda.set_device(local)
+        return tc_at_wall(W, args.tc_at_wall, local, args.tc_scale)
+
     import torch
     torch.cuda.set_device(local)
     dist = None
@@ -314,6 +390,7 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     kernel_s, launches = 0.0, 0
+    phase = dict(kernel_s=0.0, gather_s=0.0, resample_s=0.0, run_s=0.0)
     tot = dict(proposals=0, accepts=0, visits=0, chunks=0, chunks_acc=0, slice_proposals=0)
     for k in range(args.steps):
         flush.zero_()
@@ -322,6 +399,8 @@ def main():
         sess.run()
         evs[k][1].record(stream)
         st = sess.stats()
+        for key, v in sess.timing().items():
+            phase[key] += v
         kernel_s += st["kernel_s"]
         launches += st["launches"]
         for key in tot:
@@ -331,10 +410,14 @@ def main():
         dist.barrier()
     clocks = clk.stop()
     t_rank = sum(a.elapsed_time(b) for a, b in evs) / 1e3
-    t = torch.tensor([t_rank, kernel_s], dtype=torch.float64, device="cuda")
+    t = torch.tensor([t_rank, kernel_s, phase["gather_s"], phase["resample_s"]], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     T, KS = float(t[0]), float(t[1])
+    # where a step's time goes (max over ranks, per step): sweep kernels, energy gathers (NCCL allgather on
+    # several GPUs) and population steps (record exchange) of the level-by-level schemes
+    step_split = {"kernel_ms": 1e3 * KS / args.steps, "gather_ms": 1e3 * float(t[2]) / args.steps,
+                  "resample_ms": 1e3 * float(t[3]) / args.steps, "step_ms": 1e3 * T / args.steps}
     rc, res = sess.result()
     sess.close()
     vps = visits_per_step(W, world)
@@ -417,6 +500,7 @@ def main():
                 "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.e2e_steps),
                         "d2h_bytes_per_step": d2h // max(1, args.e2e_steps)},
                 "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+                "step_split": step_split,
                 "best_tc": res["tc"], "best_sc": res["sc"], "valid": bool(res["valid"] and res["labels_ok"])}
         print(json.dumps(line), flush=True)
     if dist:

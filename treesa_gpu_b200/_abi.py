@@ -68,7 +68,7 @@ TRACE_COLS = ["t", "level", "beta", "best_lcost_per_slice", "best_sc", "mean_E",
               "best_nsliced", "mean_nsliced"]
 
 EXPORTS = ["tsa_abi_version", "tsa_run", "tsa_result_free", "tsa_session_create", "tsa_session_run",
-           "tsa_session_result", "tsa_session_reset", "tsa_session_destroy", "tsa_session_stats",
+           "tsa_session_result", "tsa_session_reset", "tsa_session_destroy", "tsa_session_stats", "tsa_session_timing",
            "tsa_session_energies", "tsa_session_chains", "tsa_nccl_unique_id", "tsa_session_info",
            "tsa_resample", "tsa_resample_noalloc", "tsa_release_cached_memory", "tsa_abi_sizes"]
 
@@ -212,6 +212,7 @@ def lib():
     L.tsa_session_destroy.argtypes = [C.c_void_p]
     L.tsa_session_destroy.restype = None
     L.tsa_session_stats.argtypes = [C.c_void_p, C.POINTER(C.c_uint64), C.POINTER(C.c_double)]
+    L.tsa_session_timing.argtypes = [C.c_void_p, C.POINTER(C.c_double)]
     L.tsa_session_energies.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_int32),
                                        C.POINTER(C.c_int32), C.c_char_p, C.c_size_t]
     L.tsa_session_chains.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.c_char_p,

@@ -286,18 +286,18 @@ int Comm::resample(const int* anc, uint8_t* d_rec, uint8_t* d_rec2, int* d_anc, 
                     recv_ids.data());
   const int nsend = send_off[world], nrecv = recv_off[world];
   int rc = grow(&p->sendbuf, &p->send_cap, (size_t)std::max(1, nsend) * rb, err, errlen);
-  if (!rc) rc = grow(&p->recvbuf, &p->recv_cap, (size_t)(nloc + std::max(1, nrecv)) * rb, err, errlen);
+  if (!rc) rc = grow(&p->recvbuf, &p->recv_cap, (size_t)std::max(1, nrecv) * rb, err, errlen);
   size_t icap = (size_t)p->idx_cap;
   if (!rc) rc = grow(&p->d_idx, &icap, (size_t)std::max(1, nsend), err, errlen);
   if (rc) return rc;
   p->idx_cap = (int)icap;
   // pack the records other ranks need, exchange them, then gather the new local population from
-  // [local records | received records]
+  // [local records ++ received records] (two sources, one gather kernel)
   if (nsend > 0) {
     CCK(cudaMemcpyAsync(p->d_idx, send_idx.data(), nsend * sizeof(int), cudaMemcpyHostToDevice, st));
     CCK(launch_copy_chains(d_rec, p->sendbuf, p->d_idx, nsend, rb, st));
   }
-  uint8_t* recv_base = p->recvbuf + (size_t)nloc * rb;
+  uint8_t* recv_base = p->recvbuf;
   NCK(p->N->groupStart());
   for (int q = 0; q < world; q++) {
     if (q == rank) continue;
@@ -306,10 +306,8 @@ int Comm::resample(const int* anc, uint8_t* d_rec, uint8_t* d_rec2, int* d_anc, 
     if (nr > 0) NCK(p->N->recv(recv_base + (size_t)recv_off[q] * rb, (size_t)nr * rb, ncclUint8, q, p->comm, st));
   }
   NCK(p->N->groupEnd());
-  // the local records go in front of the received ones so that src_of indexes one contiguous buffer
-  CCK(cudaMemcpyAsync(p->recvbuf, d_rec, (size_t)nloc * rb, cudaMemcpyDeviceToDevice, st));
   CCK(cudaMemcpyAsync(d_anc, src_of.data(), nloc * sizeof(int), cudaMemcpyHostToDevice, st));
-  CCK(launch_copy_chains(p->recvbuf, d_rec2, d_anc, nloc, rb, st));
+  CCK(launch_copy_chains2(d_rec, nloc, recv_base, d_rec2, d_anc, nloc, rb, st));
   CCK(cudaStreamSynchronize(st));
   return TSA_OK;
 }

@@ -521,6 +521,9 @@ struct tsa_session {
   uint32_t* d_scratch = nullptr;  // [nchains][nint] slice-move cost scratch (plan gmeta 2 only)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   cudaEvent_t evk[4] = {nullptr, nullptr, nullptr, nullptr};  // kernel start/end, two level parities
+  // level-by-level runs: end of the energy gather, start and end of the population step
+  cudaEvent_t evx[3] = {nullptr, nullptr, nullptr};
+  double gather_ms = 0, resample_ms = 0;
   cudaEvent_t eve[2] = {nullptr, nullptr};                    // energies of a level on the host
   cudaStream_t cst = nullptr;                                 // energy gathers and best-record copies
   cudaEvent_t evdone[2] = {nullptr, nullptr};                 // a level's kernel has finished (on st)
@@ -556,6 +559,8 @@ struct tsa_session {
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (auto& e : evk)
+      if (e) cudaEventDestroy(e);
+    for (auto& e : evx)
       if (e) cudaEventDestroy(e);
     for (auto& e : eve)
       if (e) cudaEventDestroy(e);
@@ -618,6 +623,7 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
   CKR(pool_alloc(1, &s->h_ns, 2 * (size_t)s->nglobal * sizeof(int)));
   CKR(pool_alloc(1, &s->h_best, s->L.rec_bytes));
   for (auto& e : s->evk) CKR(cudaEventCreate(&e));
+  for (auto& e : s->evx) CKR(cudaEventCreate(&e));
   for (auto& e : s->eve) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : s->evdone) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : s->evfree) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -704,6 +710,7 @@ int reset_run_state(tsa_session* s, char* err, size_t errlen) {
   s->best_chain = s->best_level = -1;
   s->nresample = 0;
   s->kernel_ms = 0;
+  s->gather_ms = s->resample_ms = 0;
   s->t_anneal = 0;
   s->sweep_ctr = 0;
   s->best.clear();
@@ -1124,6 +1131,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     return true;
   };
   int rc = TSA_OK;
+  bool resample_pending = false;  // a population step's events await their elapsed time
   uint8_t* buf[2] = {s->d_rec, s->d_rec2};
   if (pipelined) {
     long pend = -1;  // evaluated level whose energies are in flight
@@ -1233,11 +1241,21 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         rc = gather(0, s->st);
         if (rc) break;
         s->d2h += (size_t)nch * 12;
+        CKR(cudaEventRecord(s->evx[0], s->st));
       }
       CKR(cudaStreamSynchronize(s->st));
       float ms = 0;
       CKR(cudaEventElapsedTime(&ms, s->evk[0], s->evk[1]));
       s->kernel_ms += ms;
+      if (resample_pending) {  // the previous level's population step, complete by now
+        CKR(cudaEventElapsedTime(&ms, s->evx[1], s->evx[2]));
+        s->resample_ms += ms;
+        resample_pending = false;
+      }
+      if (eval) {
+        CKR(cudaEventElapsedTime(&ms, s->evk[1], s->evx[0]));
+        s->gather_ms += ms;
+      }
       if ((rc = check_err())) break;
       if (!eval) continue;
       const float* glc = s->h_lc;
@@ -1282,6 +1300,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         for (int q = 0; q < nrep; q++) anc[idx[ng - 1 - q]] = idx[q];
       }
       uint8_t* other = s->d_cur == s->d_rec ? s->d_rec2 : s->d_rec;
+      CKR(cudaEventRecord(s->evx[1], s->st));
       if (s->world > 1) {
         rc = s->comm->resample(anc.data(), s->d_cur, other, s->d_anc, nch, rb, s->st, err, errlen);
         if (rc) break;
@@ -1290,6 +1309,8 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         s->h2d += nch * sizeof(int);
         CKR(tsa::launch_copy_chains(s->d_cur, other, s->d_anc, nch, rb, s->st));
       }
+      CKR(cudaEventRecord(s->evx[2], s->st));
+      resample_pending = true;
       s->d_cur = other;
       std::vector<int> nfm(ng);
       for (int c = 0; c < ng; c++) nfm[c] = family[anc[c]];
@@ -1300,6 +1321,11 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   if (rc) return rc;
   CKR(cudaStreamSynchronize(s->st));
   CKR(cudaStreamSynchronize(s->cst));
+  if (resample_pending) {
+    float ms = 0;
+    CKR(cudaEventElapsedTime(&ms, s->evx[1], s->evx[2]));
+    s->resample_ms += ms;
+  }
   if ((rc = check_err())) return rc;
   if (local && (rc = reduce_local())) return rc;
   memcpy(s->best.data(), s->h_best, rb);
@@ -1427,6 +1453,15 @@ int tsa_run(const tsa_instance* inst, const tsa_options* opt, tsa_result* res, c
   if (rc == TSA_ERR_INVALID) set_err(err, errlen, "final tree invalid or labels mismatch");
   tsa_session_destroy(s);
   return rc;
+}
+
+int tsa_session_timing(tsa_session* s, double* t4) {
+  if (!s || !t4) return TSA_ERR_ARG;
+  t4[0] = s->kernel_ms / 1e3;
+  t4[1] = s->gather_ms / 1e3;
+  t4[2] = s->resample_ms / 1e3;
+  t4[3] = s->t_anneal;
+  return TSA_OK;
 }
 
 int tsa_session_stats(tsa_session* s, uint64_t* c12, double* ksec) {

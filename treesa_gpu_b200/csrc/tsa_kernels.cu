@@ -2484,6 +2484,15 @@ __global__ void k_copy(const uint4* __restrict__ src, uint4* __restrict__ dst, c
   uint4* d = dst + (size_t)blockIdx.x * n4;
   for (int i = threadIdx.x; i < n4; i += blockDim.x) d[i] = s[i];
 }
+// The same gather from two sources: record k of [a (na records) ++ b] (a multi-GPU resampling step: the
+// rank's own records, then the ones it received), without first copying a and b into one buffer.
+__global__ void k_copy2(const uint4* __restrict__ a, int na, const uint4* __restrict__ b, uint4* __restrict__ dst,
+                        const int* __restrict__ idx, int n4) {
+  const int k = idx[blockIdx.x];
+  const uint4* s = k < na ? a + (size_t)k * n4 : b + (size_t)(k - na) * n4;
+  uint4* d = dst + (size_t)blockIdx.x * n4;
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) d[i] = s[i];
+}
 
 // ------------------------------------------------------------------------------------------------
 // Host side: plans and launches
@@ -2691,6 +2700,14 @@ cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc,
   if (nchains <= 0) return cudaSuccess;
   k_copy<<<nchains, 256, 0, st>>>(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), anc,
                                   (int)(rec_bytes / 16));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_copy_chains2(const uint8_t* a, int na, const uint8_t* b, uint8_t* dst, const int* idx, int nchains,
+                                uint32_t rec_bytes, cudaStream_t st) {
+  if (nchains <= 0) return cudaSuccess;
+  k_copy2<<<nchains, 256, 0, st>>>(reinterpret_cast<const uint4*>(a), na, reinterpret_cast<const uint4*>(b),
+                                   reinterpret_cast<uint4*>(dst), idx, (int)(rec_bytes / 16));
   return cudaGetLastError();
 }
 

@@ -87,6 +87,9 @@ cudaError_t plan_sweeps(const Layout& L, int nchains, int device, int hint, int 
 cudaError_t launch_sweeps(const SweepArgs& a, const LaunchPlan& plan, cudaStream_t st);
 cudaError_t launch_copy_chains(const uint8_t* src, uint8_t* dst, const int* anc, int nchains, uint32_t rec_bytes,
                                cudaStream_t st);
+// dst record c <- record idx[c] of [a (na records) ++ b]
+cudaError_t launch_copy_chains2(const uint8_t* a, int na, const uint8_t* b, uint8_t* dst, const int* idx, int nchains,
+                                uint32_t rec_bytes, cudaStream_t st);
 cudaError_t upload_lse_table(const float* host64, float* dev64, cudaStream_t st);
 int fixup_count();
 cudaError_t expf_selftest(uint32_t lo, uint32_t hi, unsigned long long* d_sum, unsigned int* d_err, cudaStream_t st);

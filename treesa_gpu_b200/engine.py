@@ -96,6 +96,13 @@ class Session:
         d["kernel_s"] = ks.value
         return d
 
+    def timing(self):
+        """Seconds of the last run on this rank: sweep kernels, energy gathers and population steps (device
+        time of level-by-level runs) and the whole call's wall time (tsa_session_timing)."""
+        t = (C.c_double * 4)()
+        self.L.tsa_session_timing(self.h, t)
+        return dict(zip(["kernel_s", "gather_s", "resample_s", "run_s"], [float(x) for x in t]))
+
     def energies(self):
         lc = np.zeros(self.nchains, np.float32)
         sc = np.zeros(self.nchains, np.int32)
