@@ -1193,6 +1193,10 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
 // the CTA's threads (see par_phase_flat); these are its per-batch tables.
 constexpr int kFlatBatch = 512;            // nodes per batch (one owner thread each)
 constexpr int kFlatItems = 8192;           // (node, chunk) items per window
+// a batch of at most kFlatDirect items per thread decodes each item's node by a binary search over the
+// owners' item offsets; larger batches build the item list first (flat_build).  Measured on C3/C4: 2
+// against 1 and 0 (always the list), 1 % and 2-4 % faster.
+constexpr int kFlatDirect = 2;
 constexpr uint32_t kLeafSumCache = 220u << 10;  // cache leaf summaries in shared memory below this total
 
 struct BlockSmem {
@@ -1791,29 +1795,32 @@ __device__ __forceinline__ Item flat_decode(const FlatTabs& F, int nb, int e) {
 
 // The items numbered [w0, w0 + kFlatItems) into F.items.  A warp whose owners have fewer than 32 chunks
 // each lets every owner write its own items (as many steps as the widest owner has chunks); otherwise
-// the warp expands the masks of its 32 owners together: for owner o, lane l writes the item of chunk l
-// (and 32 + l) if that bit is set, at the owner's offset plus the number of set bits below it.
+// the warp expands the masks of its 32 owners together: for owner o (mask and offset broadcast from its
+// lane), lane l writes the item of chunk l (and 32 + l) if that bit is set, at the owner's offset plus
+// the number of set bits below it.
 __device__ __forceinline__ void flat_build(const FlatTabs& F, int nb, int w0) {
   const int tid = threadIdx.x, lane = tid & 31, wbase = tid & ~31;
   const uint32_t lt = (1u << lane) - 1u;
+  const unsigned FULL = 0xFFFFFFFFu;
   const uint64_t myu = tid < nb ? F.u[tid] : 0ull;
+  const int myoff = (int)(tid < nb ? F.off[tid] : 0u) - w0;
   int wide = __popcll(myu);
-  for (int o = 16; o > 0; o >>= 1) wide = max(wide, __shfl_xor_sync(0xFFFFFFFFu, wide, o));
+  for (int o = 16; o > 0; o >>= 1) wide = max(wide, __shfl_xor_sync(FULL, wide, o));
   if (wide < 32) {
     uint64_t uu = myu;
-    for (int k = (int)(tid < nb ? F.off[tid] : 0) - w0; uu; k++) {
+    for (int k = myoff; uu; k++) {
       const int c = __ffsll((long long)uu) - 1;
       uu &= uu - 1;
       if (k >= 0 && k < kFlatItems) F.items[k] = ((uint32_t)tid << 16) | (uint32_t)c;
     }
     return;
   }
-  for (int o = 0; o < 32; o++) {
+  const int nown = min(32, nb - wbase);  // warp-uniform
+  for (int o = 0; o < nown; o++) {
     const int j = wbase + o;
-    if (j >= nb) break;
-    const uint64_t u = F.u[j];
+    const uint64_t u = __shfl_sync(FULL, myu, o);
+    const int base = __shfl_sync(FULL, myoff, o);
     if (!u) continue;
-    const int base = (int)F.off[j] - w0;
     const uint32_t lo = (uint32_t)u, hi = (uint32_t)(u >> 32);
     const int klo = base + __popc(lo & lt), khi = base + __popc(lo) + __popc(hi & lt);
     if (((lo >> lane) & 1u) && klo >= 0 && klo < kFlatItems) F.items[klo] = ((uint32_t)j << 16) | (uint32_t)lane;
@@ -1946,7 +1953,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
     if (tid < nb) F.off[tid] = (uint32_t)(incl - nck + before);
     __syncthreads();
     // 3. counts of every item, in windows of kFlatItems; a thread keeps X of its first IPT items.  A batch
-    // of at most IPT * T items decodes each item's node and chunk directly (no list)
+    // of at most min(IPT, kFlatDirect) T items decodes each item's node and chunk directly (no list)
     Item kk[IPT];
     ulonglong2 kx[IPT];
 #pragma unroll
@@ -1954,7 +1961,7 @@ __device__ void par_phase_flat(const BlkCtx& B, const FlatTabs& F, uint16_t* wl,
       kk[i] = Item{-1, 0};
       kx[i] = make_ulonglong2(0ull, 0ull);
     }
-    const bool direct = total <= IPT * T;
+    const bool direct = total <= min(IPT, kFlatDirect) * T;
     for (int w0 = 0; w0 < total; w0 += kFlatItems) {
       if (!direct) {
         if (w0) __syncthreads();  // the previous window's items are consumed
