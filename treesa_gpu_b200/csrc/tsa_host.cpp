@@ -524,6 +524,7 @@ struct tsa_session {
   // level-by-level runs: end of the energy gather, start and end of the population step
   cudaEvent_t evx[3] = {nullptr, nullptr, nullptr};
   double gather_ms = 0, resample_ms = 0;
+  double host_s = 0, fetch_s = 0;  // host selection work; best-record fetches (copy or NCCL broadcast)
   cudaEvent_t eve[2] = {nullptr, nullptr};                    // energies of a level on the host
   cudaStream_t cst = nullptr;                                 // energy gathers and best-record copies
   cudaEvent_t evdone[2] = {nullptr, nullptr};                 // a level's kernel has finished (on st)
@@ -711,6 +712,7 @@ int reset_run_state(tsa_session* s, char* err, size_t errlen) {
   s->nresample = 0;
   s->kernel_ms = 0;
   s->gather_ms = s->resample_ms = 0;
+  s->host_s = s->fetch_s = 0;
   s->t_anneal = 0;
   s->sweep_ctr = 0;
   s->best.clear();
@@ -1261,25 +1263,32 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       const float* glc = s->h_lc;
       const int *gsc = s->h_sc, *gns = s->h_ns;
       int improved;
+      double th = now_s();
       if (local)
         process_local(lev, 0, &improved);
       else
         process(lev, glc, gsc, gns, &improved);
+      s->host_s += now_s() - th;
       if (improved >= 0) {
+        th = now_s();
         if ((rc = fetch_best(improved, s->d_cur, s->st))) break;
         CKR(cudaStreamSynchronize(s->st));
+        s->fetch_s += now_s() - th;
       }
       if (last || switching || s->scheme == TSA_SCHEME_INDEP) continue;
+      th = now_s();
       std::vector<int> anc(ng);
+      std::vector<double> E(ng);  // every chain's energy, computed once (the same doubles as per use)
+      for (int c = 0; c < ng; c++) E[c] = s->energyE(glc[c], gsc[c], gns[c]);
       if (s->scheme == TSA_SCHEME_PA) {  // :1837-1856
         double db = s->betas[lev + 1] - beta_last;
         beta_last = s->betas[lev + 1];
         std::vector<double> w(ng);
         double Emin = INFINITY;
-        for (int c = 0; c < ng; c++) Emin = std::min(Emin, s->energyE(glc[c], gsc[c], gns[c]));
+        for (int c = 0; c < ng; c++) Emin = std::min(Emin, E[c]);
         double wsum = 0;
         for (int c = 0; c < ng; c++) {
-          w[c] = exp(-db * (s->energyE(glc[c], gsc[c], gns[c]) - Emin));
+          w[c] = exp(-db * (E[c] - Emin));
           wsum += w[c];
         }
         double u = std::uniform_real_distribution<double>(0, 1)(hrng), acc = 0;
@@ -1292,14 +1301,13 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       } else {  // truncation, :1857-1869
         std::vector<int> idx(ng);
         std::iota(idx.begin(), idx.end(), 0);
-        std::sort(idx.begin(), idx.end(), [&](int x, int y) {
-          return s->energyE(glc[x], gsc[x], gns[x]) < s->energyE(glc[y], gsc[y], gns[y]);
-        });
+        std::sort(idx.begin(), idx.end(), [&](int x, int y) { return E[x] < E[y]; });
         std::iota(anc.begin(), anc.end(), 0);
         int nrep = (int)(s->trunc_frac * ng);
         for (int q = 0; q < nrep; q++) anc[idx[ng - 1 - q]] = idx[q];
       }
       uint8_t* other = s->d_cur == s->d_rec ? s->d_rec2 : s->d_rec;
+      s->host_s += now_s() - th;
       CKR(cudaEventRecord(s->evx[1], s->st));
       if (s->world > 1) {
         rc = s->comm->resample(anc.data(), s->d_cur, other, s->d_anc, nch, rb, s->st, err, errlen);
@@ -1455,12 +1463,14 @@ int tsa_run(const tsa_instance* inst, const tsa_options* opt, tsa_result* res, c
   return rc;
 }
 
-int tsa_session_timing(tsa_session* s, double* t4) {
-  if (!s || !t4) return TSA_ERR_ARG;
-  t4[0] = s->kernel_ms / 1e3;
-  t4[1] = s->gather_ms / 1e3;
-  t4[2] = s->resample_ms / 1e3;
-  t4[3] = s->t_anneal;
+int tsa_session_timing(tsa_session* s, double* t6) {
+  if (!s || !t6) return TSA_ERR_ARG;
+  t6[0] = s->kernel_ms / 1e3;
+  t6[1] = s->gather_ms / 1e3;
+  t6[2] = s->resample_ms / 1e3;
+  t6[3] = s->t_anneal;
+  t6[4] = s->host_s;
+  t6[5] = s->fetch_s;
   return TSA_OK;
 }
 
