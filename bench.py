@@ -390,7 +390,8 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     kernel_s, launches = 0.0, 0
-    phase = dict(kernel_s=0.0, gather_s=0.0, resample_s=0.0, run_s=0.0, select_s=0.0, fetch_s=0.0)
+    phase = dict(kernel_s=0.0, gather_s=0.0, resample_s=0.0, run_s=0.0, select_s=0.0, fetch_s=0.0, sent_bytes=0.0,
+                 recv_bytes=0.0)
     tot = dict(proposals=0, accepts=0, visits=0, chunks=0, chunks_acc=0, slice_proposals=0)
     for k in range(args.steps):
         flush.zero_()
@@ -410,8 +411,8 @@ def main():
         dist.barrier()
     clocks = clk.stop()
     t_rank = sum(a.elapsed_time(b) for a, b in evs) / 1e3
-    t = torch.tensor([t_rank, kernel_s, phase["gather_s"], phase["resample_s"], phase["select_s"], phase["fetch_s"]],
-                     dtype=torch.float64, device="cuda")
+    t = torch.tensor([t_rank, kernel_s, phase["gather_s"], phase["resample_s"], phase["select_s"], phase["fetch_s"],
+                      phase["sent_bytes"]], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     T, KS = float(t[0]), float(t[1])
@@ -419,7 +420,8 @@ def main():
     # several GPUs) and population steps (record exchange) of the level-by-level schemes
     step_split = {"kernel_ms": 1e3 * KS / args.steps, "gather_ms": 1e3 * float(t[2]) / args.steps,
                   "resample_ms": 1e3 * float(t[3]) / args.steps, "select_ms": 1e3 * float(t[4]) / args.steps,
-                  "fetch_ms": 1e3 * float(t[5]) / args.steps, "step_ms": 1e3 * T / args.steps}
+                  "fetch_ms": 1e3 * float(t[5]) / args.steps, "step_ms": 1e3 * T / args.steps,
+                  "records_sent_MB_per_level_max_rank": float(t[6]) / args.steps / len(W["betas"]) / 1e6}
     rc, res = sess.result()
     sess.close()
     vps = visits_per_step(W, world)

@@ -172,15 +172,16 @@ void tsa_session_destroy(tsa_session* s);
  * the summed device time of the sweep kernels (this rank). */
 int tsa_session_stats(tsa_session* s, uint64_t* counters12, double* kernel_seconds);
 
-/* Where the last tsa_session_run spent its time on this rank, in seconds: t6[0] the sweep kernels, t6[1]
+/* Where the last tsa_session_run spent its time on this rank, in seconds: t8[0] the sweep kernels, t8[1]
  * the energy gathers of runs that select level by level (population annealing, truncation, staged runs:
  * the device copy, or on several GPUs the NCCL allgather, which also waits for the slowest rank's sweeps),
- * t6[2] their population steps (the record gather, and on several GPUs the packing and the NCCL
- * send/receive of records), all three device time; t6[3] the wall time of the whole call; t6[4] host time
- * of the selection (scores, best tracking, ancestors); t6[5] wall time of fetching improved best records
- * (a copy, or an NCCL broadcast from the owner).  No counterpart in the reference, which reports only its
- * kernel time (csrc/treesa_gpu.cu:1908). */
-int tsa_session_timing(tsa_session* s, double* t6);
+ * t8[2] their population steps (the record gather, and on several GPUs the packing and the NCCL
+ * send/receive of records), all three device time; t8[3] the wall time of the whole call; t8[4] host time
+ * of the selection (scores, best tracking, ancestors); t8[5] wall time of fetching improved best records
+ * (a copy, or an NCCL broadcast from the owner); t8[6] / t8[7] bytes of chain records this rank sent to /
+ * received from other ranks in population steps.  No counterpart in the reference, which reports only
+ * its kernel time (csrc/treesa_gpu.cu:1908). */
+int tsa_session_timing(tsa_session* s, double* t8);
 
 /* Population resampling of caller-held chain records (the reference's Runner::resample,
  * csrc/treesa_gpu.cu:1925-1933, and its k_copy, :1017-1022): every record c becomes a copy of record

@@ -285,6 +285,8 @@ int Comm::resample(const int* anc, uint8_t* d_rec, uint8_t* d_rec2, int* d_anc, 
   tsa_resample_plan(anc, nloc, rank, world, src_of.data(), send_off.data(), send_idx.data(), recv_off.data(),
                     recv_ids.data());
   const int nsend = send_off[world], nrecv = recv_off[world];
+  sent_bytes += (uint64_t)nsend * rb;
+  recv_bytes += (uint64_t)nrecv * rb;
   int rc = grow(&p->sendbuf, &p->send_cap, (size_t)std::max(1, nsend) * rb, err, errlen);
   if (!rc) rc = grow(&p->recvbuf, &p->recv_cap, (size_t)std::max(1, nrecv) * rb, err, errlen);
   size_t icap = (size_t)p->idx_cap;

@@ -31,6 +31,8 @@ struct Comm {
   int resample(const int* anc_global, uint8_t* d_rec, uint8_t* d_rec2, int* d_anc, int nloc, uint32_t rec_bytes,
                cudaStream_t st, char* err, size_t errlen);
   int sum_u64(uint64_t* host_vals, int n, cudaStream_t st, char* err, size_t errlen);
+  // record bytes this rank has sent to / received from other ranks in population steps
+  uint64_t sent_bytes = 0, recv_bytes = 0;
   // synchronous: n doubles from every rank, in rank order, into host_out[world*n]
   int allgather_host(const double* host_in, int n, double* host_out, cudaStream_t st, char* err, size_t errlen);
   // synchronous: the owner's host buffer copied into every rank's host buffer

@@ -525,6 +525,7 @@ struct tsa_session {
   cudaEvent_t evx[3] = {nullptr, nullptr, nullptr};
   double gather_ms = 0, resample_ms = 0;
   double host_s = 0, fetch_s = 0;  // host selection work; best-record fetches (copy or NCCL broadcast)
+  uint64_t comm_sent0 = 0, comm_recv0 = 0;  // the communicator's record byte counts when the run began
   cudaEvent_t eve[2] = {nullptr, nullptr};                    // energies of a level on the host
   cudaStream_t cst = nullptr;                                 // energy gathers and best-record copies
   cudaEvent_t evdone[2] = {nullptr, nullptr};                 // a level's kernel has finished (on st)
@@ -713,6 +714,10 @@ int reset_run_state(tsa_session* s, char* err, size_t errlen) {
   s->kernel_ms = 0;
   s->gather_ms = s->resample_ms = 0;
   s->host_s = s->fetch_s = 0;
+  if (s->comm) {
+    s->comm_sent0 = s->comm->sent_bytes;
+    s->comm_recv0 = s->comm->recv_bytes;
+  }
   s->t_anneal = 0;
   s->sweep_ctr = 0;
   s->best.clear();
@@ -1463,14 +1468,20 @@ int tsa_run(const tsa_instance* inst, const tsa_options* opt, tsa_result* res, c
   return rc;
 }
 
-int tsa_session_timing(tsa_session* s, double* t6) {
-  if (!s || !t6) return TSA_ERR_ARG;
+int tsa_session_timing(tsa_session* s, double* t8) {
+  if (!s || !t8) return TSA_ERR_ARG;
+  double* t6 = t8;
+  t8[6] = t8[7] = 0;
   t6[0] = s->kernel_ms / 1e3;
   t6[1] = s->gather_ms / 1e3;
   t6[2] = s->resample_ms / 1e3;
   t6[3] = s->t_anneal;
   t6[4] = s->host_s;
   t6[5] = s->fetch_s;
+  if (s->comm) {
+    t8[6] = (double)(s->comm->sent_bytes - s->comm_sent0);
+    t8[7] = (double)(s->comm->recv_bytes - s->comm_recv0);
+  }
   return TSA_OK;
 }
 

@@ -98,11 +98,12 @@ class Session:
 
     def timing(self):
         """Seconds of the last run on this rank: sweep kernels, energy gathers and population steps (device
-        time of level-by-level runs), the whole call's wall time, host selection and best-record fetches
-        (tsa_session_timing)."""
-        t = (C.c_double * 6)()
+        time of level-by-level runs), the whole call's wall time, host selection and best-record fetches;
+        and the record bytes sent to / received from other ranks (tsa_session_timing)."""
+        t = (C.c_double * 8)()
         self.L.tsa_session_timing(self.h, t)
-        return dict(zip(["kernel_s", "gather_s", "resample_s", "run_s", "select_s", "fetch_s"], [float(x) for x in t]))
+        return dict(zip(["kernel_s", "gather_s", "resample_s", "run_s", "select_s", "fetch_s", "sent_bytes",
+                         "recv_bytes"], [float(x) for x in t]))
 
     def energies(self):
         lc = np.zeros(self.nchains, np.float32)
