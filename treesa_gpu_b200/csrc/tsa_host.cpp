@@ -517,6 +517,7 @@ struct tsa_session {
   uint64_t* d_leaf_sum = nullptr;
   float *d_lse = nullptr, *d_lc = nullptr;
   int *d_sc = nullptr, *d_ns = nullptr, *d_anc = nullptr, *d_err = nullptr;
+  uint8_t* d_best = nullptr;  // level-by-level runs: the owner's device copy of the best record
   unsigned long long* d_stats = nullptr;
   uint32_t* d_scratch = nullptr;  // [nchains][nint] slice-move cost scratch (plan gmeta 2 only)
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -556,7 +557,7 @@ struct tsa_session {
     if (cst) cudaStreamSynchronize(cst);
     for (void* p : {(void*)d_rec, (void*)d_rec2, (void*)d_init, (void*)d_leaf, (void*)d_leaf_sum, (void*)d_lse,
                     (void*)d_scratch, (void*)d_lc, (void*)d_sc, (void*)d_ns, (void*)d_anc, (void*)d_err,
-                    (void*)d_stats, (void*)h_lc, (void*)h_sc, (void*)h_ns, (void*)h_best})
+                    (void*)d_stats, (void*)h_lc, (void*)h_sc, (void*)h_ns, (void*)h_best, (void*)d_best})
       pool_free(p);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
@@ -624,6 +625,7 @@ int init_device_state(tsa_session* s, const tsa_options* O, char* err, size_t er
   CKR(pool_alloc(1, &s->h_sc, 2 * (size_t)s->nglobal * sizeof(int)));
   CKR(pool_alloc(1, &s->h_ns, 2 * (size_t)s->nglobal * sizeof(int)));
   CKR(pool_alloc(1, &s->h_best, s->L.rec_bytes));
+  CKR(pool_alloc(0, &s->d_best, s->L.rec_bytes));
   for (auto& e : s->evk) CKR(cudaEventCreate(&e));
   for (auto& e : s->evx) CKR(cudaEventCreate(&e));
   for (auto& e : s->eve) CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -1121,6 +1123,35 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     CKR(cudaMemcpyAsync(s->h_best, buf + (size_t)(g - s->rank * nch) * rb, rb, cudaMemcpyDeviceToHost, cs));
     return TSA_OK;
   };
+  // Level-by-level runs keep an improved best record on its owner's device (a device copy, no wait) and
+  // bring it to the host only when the host needs it (a stage switch, the end of the run): one transfer
+  // instead of a broadcast and a synchronisation per improvement.  With local scoring every rank keeps
+  // its own best and copies it to the host alone (reduce_local then broadcasts the winner's).
+  bool best_pending = false;
+  int best_owner = 0;
+  auto keep_best = [&](int g) -> int {
+    best_owner = s->world > 1 && !local ? g / nch : s->rank;
+    best_pending = true;
+    if (best_owner == s->rank)
+      CKR(cudaMemcpyAsync(s->d_best, s->d_cur + (size_t)(g - s->rank * nch) * rb, rb, cudaMemcpyDeviceToDevice,
+                          s->st));
+    return TSA_OK;
+  };
+  auto materialize_best = [&]() -> int {
+    if (!best_pending) return TSA_OK;
+    const double th = now_s();
+    s->d2h += rb;
+    if (s->world > 1 && !local) {  // a collective: every rank reaches it at the same point of the run
+      const int r = s->comm->fetch_record(s->d_best, rb, best_owner, s->h_best, s->st, err, errlen);
+      if (r) return r;
+    } else {
+      CKR(cudaMemcpyAsync(s->h_best, s->d_best, rb, cudaMemcpyDeviceToHost, s->st));
+    }
+    CKR(cudaStreamSynchronize(s->st));
+    best_pending = false;
+    s->fetch_s += now_s() - th;
+    return TSA_OK;
+  };
   auto check_err = [&]() -> int {
     int herr = 0;
     CKR(cudaMemcpy(&herr, s->d_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1219,6 +1250,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
         // stage switch (:1789-1799): the incumbent, rescored in the new energy, stays the best until beaten
         s->cur_mode = s->lmode[lev];
         if (s->best_chain >= 0) {
+          if ((rc = materialize_best())) break;
           const uint8_t* br = s->h_best;
           HostE H1 = host_energy(s->I, s->models, reinterpret_cast<const uint64_t*>(br),
                                  reinterpret_cast<const uint32_t*>(br + s->L.off_ch),
@@ -1274,12 +1306,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       else
         process(lev, glc, gsc, gns, &improved);
       s->host_s += now_s() - th;
-      if (improved >= 0) {
-        th = now_s();
-        if ((rc = fetch_best(improved, s->d_cur, s->st))) break;
-        CKR(cudaStreamSynchronize(s->st));
-        s->fetch_s += now_s() - th;
-      }
+      if (improved >= 0 && (rc = keep_best(improved))) break;
       if (last || switching || s->scheme == TSA_SCHEME_INDEP) continue;
       th = now_s();
       std::vector<int> anc(ng);
@@ -1340,6 +1367,7 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
     s->resample_ms += ms;
   }
   if ((rc = check_err())) return rc;
+  if ((rc = materialize_best())) return rc;
   if (local && (rc = reduce_local())) return rc;
   memcpy(s->best.data(), s->h_best, rb);
   // the energies of the last level, this rank's chains
