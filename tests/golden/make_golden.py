@@ -77,6 +77,15 @@ def tree_words(t):
     return (t[:, 0] | (t[:, 1] << 16)).astype(np.uint32)
 
 
+def dump_json(obj, path):
+    """Indented JSON with every list of numbers on one line (start trees stay compact)."""
+    text = json.dumps(obj, indent=1)
+    text = re.sub(r"\[\s*([-\d.eE+,\s]+?)\s*\]", lambda mm: "[" + ", ".join(mm.group(1).split()).replace(",,", ",") + "]",
+                  text)
+    with open(path, "w") as f:
+        f.write(text)
+
+
 def digest(trees, labels):
     h = hashlib.sha256()
     h.update(np.ascontiguousarray(trees, np.uint32).tobytes())
@@ -231,8 +240,7 @@ def main(ref):
                               tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
     exp = dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes, edge=edge)
     exp["baseline"] = baseline(ref)
-    with open(os.path.join(HERE, "expected.json"), "w") as f:
-        json.dump(exp, f, indent=1)
+    dump_json(exp, os.path.join(HERE, "expected.json"))
     print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}, "
           f"variants {len(variants)}, modes {len(modes)}, edge {len(edge)}")
 
@@ -254,7 +262,6 @@ if __name__ == "__main__":
         with open(path) as f:
             exp = json.load(f)
         exp["baseline"] = baseline(ref)
-        with open(path, "w") as f:
-            json.dump(exp, f, indent=1)
+        dump_json(exp, path)
     else:
         main(ref)
