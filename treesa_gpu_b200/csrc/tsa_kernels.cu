@@ -179,6 +179,10 @@ struct WarpCtx {
   const float* lse;      // shared
   const double* exptab;  // shared: 2^(j/64)
   const uint64_t* leaf;  // shared
+  // pre-order: the sweep's random numbers of every node, drawn up front (see k_anneal_warp), word i for
+  // node m + i: bits 8..31 of Philox .y (all the Metropolis test reads) | the top two bits of .x (all
+  // the rule pick reads)
+  const uint32_t* rtab;
 };
 
 struct Counters {
@@ -311,7 +315,8 @@ struct Prop {
 };
 // MODEL: energy modes gpu / h100; the four contractions (K,M)->P, (P,O)->D, (K,O)->X, (X,M)->D are
 // counted from the label sets as the reference does (cpu_ref.h:69-72), which also needs P's set.
-template <int NW, bool MODEL = false>
+// PRE: the node's random numbers come from X_.rtab instead of a Philox call on the move's critical path.
+template <int NW, bool MODEL = false, bool PRE = false>
 __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* lab, const uint32_t* ch,
                                             const uint32_t* cz, const Set<NW>& NM, int v, uint32_t chv,
                                             uint32_t sweep, uint32_t chain) {
@@ -320,7 +325,14 @@ __device__ __forceinline__ Prop<NW> propose(const WarpCtx& X_, const uint64_t* l
   p.i = v - m;
   int l = (int)(chv & 0xFFFFu), r = (int)(chv >> 16);
   bool li = l >= m, ri = r >= m;
-  U4 rnd = philox10((uint32_t)v, sweep, chain, 0u, X_.key0, X_.key1);
+  U4 rnd;
+  if constexpr (PRE) {
+    const uint32_t pk = X_.rtab[v - m];
+    rnd.x = pk << 30;
+    rnd.y = pk & 0xFFFFFF00u;
+  } else {
+    rnd = philox10((uint32_t)v, sweep, chain, 0u, X_.key0, X_.key1);
+  }
   int rule = pick_rule(li, ri, rnd.x);
   int slotP = rule >> 1;
   int slotM = ((rule ^ (rule >> 1)) & 1) ^ 1;
@@ -391,13 +403,13 @@ __device__ __forceinline__ void apply(const Prop<NW>& p, int m, uint64_t* lab, u
   }
 }
 // propose + apply at one node; returns v's children word after the move (unchanged for a leaf-only node)
-template <int NW, bool PAR, typename C, bool MODEL = false>
+template <int NW, bool PAR, typename C, bool MODEL = false, bool PRE = false>
 __device__ __forceinline__ uint32_t visit(const WarpCtx& X_, uint64_t* lab, uint32_t* ch, uint32_t* cz,
                                           const Set<NW>& NM, uint16_t* par, int v, uint32_t sweep, uint32_t chain,
                                           C& cnt) {
   const uint32_t chv = ch[v - X_.m];
   if ((int)(chv & 0xFFFFu) < X_.m && (int)(chv >> 16) < X_.m) return chv;
-  Prop<NW> p = propose<NW, MODEL>(X_, lab, ch, cz, NM, v, chv, sweep, chain);
+  Prop<NW> p = propose<NW, MODEL, PRE>(X_, lab, ch, cz, NM, v, chv, sweep, chain);
   cnt.prop++;
   if (p.acc) {
     cnt.acc++;
@@ -707,6 +719,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
   X_.lse = s_lse;
   X_.exptab = s_exp;
   X_.leaf = s_leaf;
+  X_.rtab = nullptr;
 
   uint8_t* slot = smem + W.off_slots + (size_t)warp * W.slot_bytes;
   uint64_t* lab = reinterpret_cast<uint64_t*>(slot);
@@ -887,6 +900,15 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
         }
       } else {
         // ---- pre-order: work list of ready nodes (cpu_ref.h:89-126, k_warp :641-700) ----
+        // A node's Philox counter {node, sweep, chain} does not depend on the visiting order, so all of
+        // the sweep's draws are made up front, 32 nodes at a time, into the key array that par order
+        // alone uses: a step of the work list (one latency-bound dependent chain per sweep level of the
+        // tree) then reads one word instead of running ten Philox rounds.
+        for (int i = lane; i < nint; i += 32) {
+          const U4 r = philox10((uint32_t)(m + i), sw, chain, 0u, X_.key0, X_.key1);
+          key[i] = (r.y & 0xFFFFFF00u) | (r.x >> 30);
+        }
+        X_.rtab = key;
         if (lane == 0) wl[0] = (uint16_t)(nint - 1);
         int sp = 1;
         __syncwarp();
@@ -895,7 +917,7 @@ __global__ void __launch_bounds__(512) k_anneal_warp(SweepArgs a, int wpc) {
           int v = lane < k ? m + (int)wl[b0 + lane] : 0;
           __syncwarp();
           uint32_t cw = 0;
-          if (lane < k) cw = visit<NW, false, ChainCounters, MODEL>(X_, lab, ch, cz, NM, par, v, sw, chain, cnt);
+          if (lane < k) cw = visit<NW, false, ChainCounters, MODEL, true>(X_, lab, ch, cz, NM, par, v, sw, chain, cnt);
           // internal children become ready (one with two leaf children takes an empty visit next step)
           bool c1 = lane < k && (int)(cw & 0xFFFFu) >= m;
           bool c2 = lane < k && (int)(cw >> 16) >= m;
@@ -1019,6 +1041,7 @@ __global__ void __launch_bounds__(896, 1) k_anneal_pair(SweepArgs a, int npairs)
   X_.lse = s_lse;
   X_.exptab = s_exp;
   X_.leaf = s_leaf;
+  X_.rtab = nullptr;
 
   uint8_t* slot = smem + W.off_slots + (size_t)pair * W.slot_bytes;
   uint64_t* lab = reinterpret_cast<uint64_t*>(slot);
