@@ -988,16 +988,24 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.scratch = s->d_scratch;
   s->best.resize(rb);
   // host side of one evaluated level: best tracking, trace, population step (returns the ancestors)
+  // every chain's score and energy of the evaluated level (the selection step reuses the energies);
+  // computed by a few host threads for large populations, then reduced in chain order as before
+  std::vector<double> SV(ng), EV(ng);
+  const int hthreads = ng >= 2048 ? std::min(4, std::max(1, omp_get_num_procs())) : 1;
   auto process = [&](size_t lev, const float* glc, const int* gsc, const int* gns, int* improved) {
+#pragma omp parallel for num_threads(hthreads) schedule(static)
+    for (int c = 0; c < ng; c++) {
+      SV[c] = s->score(glc[c], gsc[c], gns[c]);
+      EV[c] = s->energyE(glc[c], gsc[c], gns[c]);
+    }
     int bi = 0;
     double bs = INFINITY, meanE = 0, meanNs = 0;
     for (int c = 0; c < ng; c++) {
-      double sv = s->score(glc[c], gsc[c], gns[c]);
-      if (sv < bs) {
-        bs = sv;
+      if (SV[c] < bs) {
+        bs = SV[c];
         bi = c;
       }
-      meanE += s->energyE(glc[c], gsc[c], gns[c]);
+      meanE += EV[c];
       meanNs += gns[c];
     }
     meanE /= ng;
@@ -1310,19 +1318,17 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
       if (last || switching || s->scheme == TSA_SCHEME_INDEP) continue;
       th = now_s();
       std::vector<int> anc(ng);
-      std::vector<double> E(ng);  // every chain's energy, computed once (the same doubles as per use)
-      for (int c = 0; c < ng; c++) E[c] = s->energyE(glc[c], gsc[c], gns[c]);
+      const std::vector<double>& E = EV;  // every chain's energy at this level (process)
       if (s->scheme == TSA_SCHEME_PA) {  // :1837-1856
         double db = s->betas[lev + 1] - beta_last;
         beta_last = s->betas[lev + 1];
         std::vector<double> w(ng);
         double Emin = INFINITY;
         for (int c = 0; c < ng; c++) Emin = std::min(Emin, E[c]);
+#pragma omp parallel for num_threads(hthreads) schedule(static)
+        for (int c = 0; c < ng; c++) w[c] = exp(-db * (E[c] - Emin));
         double wsum = 0;
-        for (int c = 0; c < ng; c++) {
-          w[c] = exp(-db * (E[c] - Emin));
-          wsum += w[c];
-        }
+        for (int c = 0; c < ng; c++) wsum += w[c];
         double u = std::uniform_real_distribution<double>(0, 1)(hrng), acc = 0;
         int j = 0;
         for (int c = 0; c < ng; c++) {
