@@ -987,11 +987,11 @@ int tsa_session_run(tsa_session* s, char* err, size_t errlen) {
   a.leaf_sum = s->d_leaf_sum;
   a.scratch = s->d_scratch;
   s->best.resize(rb);
-  // host side of one evaluated level: best tracking, trace, population step (returns the ancestors)
-  // every chain's score and energy of the evaluated level (the selection step reuses the energies);
-  // computed by a few host threads for large populations, then reduced in chain order as before
+  // every chain's score and energy of the evaluated level (the selection step reuses the energies),
+  // computed by a few host threads for large populations, then reduced in chain order
   std::vector<double> SV(ng), EV(ng);
   const int hthreads = ng >= 2048 ? std::min(4, std::max(1, omp_get_num_procs())) : 1;
+  // host side of one evaluated level: best tracking and trace
   auto process = [&](size_t lev, const float* glc, const int* gsc, const int* gns, int* improved) {
 #pragma omp parallel for num_threads(hthreads) schedule(static)
     for (int c = 0; c < ng; c++) {
