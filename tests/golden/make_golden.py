@@ -1,10 +1,10 @@
 """Generate the golden fixtures of the test suite from the reference (run where the reference's source
 tree exists; the fixtures are committed and the GPU box never reads the reference).
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT] [--baseline]
+    python tests/golden/make_golden.py [REFERENCE_ROOT] [--baseline] [--instances]
 
-REFERENCE_ROOT defaults to $TREESA_REFERENCE, else BASELINE.json's "reference_path".  --baseline only
-(re)computes section (g) and keeps the rest of expected.json.
+REFERENCE_ROOT defaults to $TREESA_REFERENCE, else BASELINE.json's "reference_path".  --baseline
+(re)computes section (g), --instances section (h); either keeps the rest of expected.json.
 
 Writes
   instances.json  -- instances of the reference's tests/data (binary instance format, read_instance
@@ -32,7 +32,11 @@ Writes
                      300 x 10, par, from its 4 spectral start trees, stored here), as one digest per
                      block of 64 chains; C3 / C4 / C5 at full size on a few chains over three levels of
                      the schedule (its first, middle and last beta) x the config's sweeps, C5 with a
-                     fixed slice set.
+                     fixed slice set;
+                     (h) SHA-256 of the BASELINE instances that the reference's own generators build
+                     (bench/instances.py sat / grid_ksat, bench/large_compare.py sq, imported from its
+                     tree): C1 sat(60, 1) and C2 sat(100, 1) with labels numbered by first appearance,
+                     C4 sq(64), C5 grid_ksat(24, 4.26, 3, 1, seed=1), labels = abs(literal) - 1.
 """
 import hashlib
 import json
@@ -240,9 +244,40 @@ def main(ref):
                               tc=r["tc"], sc=r["sc"], order="par", scheme=r["scheme"]))
     exp = dict(e2e=e2e, cpuref=cpuref, large=large, variants=variants, modes=modes, edge=edge)
     exp["baseline"] = baseline(ref)
+    exp["reference_instances"] = reference_instances(ref)
     dump_json(exp, os.path.join(HERE, "expected.json"))
     print(f"instances {len(inst)}, e2e {len(e2e)}, cpuref {len(cpuref)}, large {len(large)}, "
           f"variants {len(variants)}, modes {len(modes)}, edge {len(edge)}")
+
+
+def instance_digest(ixs):
+    h = hashlib.sha256()
+    for ix in ixs:
+        h.update((",".join(str(int(l)) for l in ix) + ";").encode())
+    return h.hexdigest()
+
+
+def reference_instances(ref):
+    """Section (h): the reference's generators run from its source tree."""
+    import importlib.util
+    bench = os.path.join(ref, "bench")
+    sys.path.insert(0, bench)
+    try:
+        def load(name):
+            spec = importlib.util.spec_from_file_location("ref_" + name, os.path.join(bench, name + ".py"))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            return mod
+        inst, lc = load("instances"), load("large_compare")
+    finally:
+        sys.path.remove(bench)
+
+    def first_appearance(ixs):
+        ids = {}
+        return [[ids.setdefault(l, len(ids)) for l in ix] for ix in ixs]
+    out = {"c1": first_appearance(inst.sat(60, seed=1)[0]), "c2": first_appearance(inst.sat(100, seed=1)[0]),
+           "c4": lc.sq(64)[0], "c5": [[abs(l) - 1 for l in c] for c in inst.grid_ksat(24, 4.26, 3, 1, seed=1)[0]]}
+    return {k: dict(m=len(v), sha256=instance_digest(v)) for k, v in out.items()}
 
 
 def reference_root(argv):
@@ -257,11 +292,13 @@ def reference_root(argv):
 
 if __name__ == "__main__":
     ref = reference_root(sys.argv[1:])
-    if "--baseline" in sys.argv:
+    if "--baseline" in sys.argv or "--instances" in sys.argv:
         path = os.path.join(HERE, "expected.json")
         with open(path) as f:
             exp = json.load(f)
-        exp["baseline"] = baseline(ref)
+        if "--baseline" in sys.argv:
+            exp["baseline"] = baseline(ref)
+        exp["reference_instances"] = reference_instances(ref)
         dump_json(exp, path)
     else:
         main(ref)

@@ -75,3 +75,17 @@ def test_oracle_reproduces_the_full_size_cpu_ref_digests(golden):
                                seed=e["seed"], sc_target=e["sc_target"], S=S)
         assert _util.digest(t, lab) == e["sha256"], e["config"]
         assert cnt[0] == e["proposals"] and cnt[1] == e["accepts"]
+
+
+def test_instances_equal_the_reference_generators_output(golden):
+    """C1, C2, C4 and C5 as the reference's own generators build them (bench/instances.py sat / grid_ksat,
+    bench/large_compare.py sq; digests made from the reference's tree by make_golden.py --instances)."""
+    import hashlib
+
+    import workloads as WL
+    for cfg, e in golden[1]["reference_instances"].items():
+        ixs, iy, nlab = WL.instance(cfg)
+        h = hashlib.sha256()
+        for ix in ixs:
+            h.update((",".join(str(int(l)) for l in ix) + ";").encode())
+        assert len(ixs) == e["m"] and h.hexdigest() == e["sha256"], cfg
